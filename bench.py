@@ -1,0 +1,552 @@
+#!/usr/bin/env python
+"""bench.py — f32 matmul 4096^2 TFLOP/s (+ streaming-kernel HBM GB/s) on 1..8 B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--mode strict|tf32x3]
+    python bench.py --impl reference ...     the reference's own CPU leg
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+One step = one pass of the matmul site C = A*B, M=N=K=4096, over resident
+A, B drawn uniform[-1,1) from seed 2 (the seeded i32-hash stream, generated
+on the device). With N GPUs the site is row-sharded: rank r owns rows
+[lo, hi) of A and C, B is replicated by an NCCL broadcast from rank 0 inside
+every step, so the total work is fixed (strong scaling). Time is taken with
+CUDA events on the launching stream, max over ranks; L2 is flushed (a
+256 MiB write) between timed steps. Rank 0 prints one JSON line.
+
+The streaming suite (saxpy, transpose, gather, sum, FIR, conv2d at 2^20
+scale, L2 flushed before every launch; and saxpy / sum / gather at 2^30,
+2^30, 2^28 sharded over the ranks) is reported under "streaming".
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import re
+import shutil
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "f32 matmul 4096² TFLOP/s + streaming-kernel HBM GB/s at 1/2/4/8 B200"
+N_MM = 4096
+SEED_MM = 2
+# The reference's published number for this metric: its rung-0 CUDA kernel,
+# N=4096 f32, FMA off (bit-exact face), 57.2 ms on an RTX 4090.
+BASELINE_TFLOPS = 2.40
+HBM_FALLBACK_GBS = 6650.0
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "sm_max_mhz": float(p.get("sm_max_mhz", 1965.0)),
+                "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": HBM_FALLBACK_GBS, "sm_max_mhz": 1965.0, "source": "fallback"}
+
+
+def host_cores() -> int:
+    n = os.cpu_count() or 1
+    try:
+        q, per = open("/sys/fs/cgroup/cpu.max").read().split()
+        if q != "max":
+            n = min(n, max(1, -(-int(q) // int(per))))
+    except Exception:
+        pass
+    return n
+
+
+def smi_device(local: int) -> str:
+    """nvidia-smi's name for CUDA device `local` (index or UUID)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        items = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(items):
+            return items[local]
+    return str(local)
+
+
+# ---- clock sampling ----------------------------------------------------------------------
+
+class Clocks:
+    """nvidia-smi sampling every 200 ms while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        if not shutil.which("nvidia-smi"):
+            return
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        self.proc = subprocess.Popen(
+            ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+             "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+
+    def stop(self) -> dict | None:
+        if not self.proc:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = list(csv.reader(io.StringIO(open(self.path).read())))
+        os.unlink(self.path)
+        sm, mx, reasons, power = [], 0.0, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1].split()[0]))
+                mx = max(mx, float(r[2].split()[0]))
+                power.append(float(r[3].split()[0]))
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        loaded = [s for s, p in zip(sm, power) if p > 250.0] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power) if power else None}
+
+
+# ---- the reference's CPU leg -----------------------------------------------------------------
+
+def cpp_mt_path() -> str:
+    return os.path.join(ROOT, "oracle", "_ref", "cpp_mt")
+
+
+def run_cpp_mt(n: int, iters: int, threads: int, timeout: float = 300.0) -> dict:
+    """Time benches/matmul/cpp_mt.cpp (the reference's threaded C++ matmul leg,
+    compiled unmodified by oracle/Makefile) on this host's cores."""
+    env = dict(os.environ, THREADS=str(threads))
+    out = subprocess.run([cpp_mt_path(), str(n), str(iters), "f32"], capture_output=True, text=True,
+                         env=env, timeout=timeout, check=True).stdout
+    m = re.search(r"N=(\d+) ([\d.]+) ms ([\d.]+) GFLOP/s c0=(-?[\d.]+) clast=(-?[\d.]+) T=(\d+)", out)
+    if not m:
+        raise RuntimeError(f"unexpected cpp_mt output: {out!r}")
+    ms = float(m.group(2))
+    return {"ms": ms, "tflops": 2.0 * n ** 3 / (ms * 1e-3) / 1e12, "threads": int(m.group(6)),
+            "c0": float(m.group(4)), "clast": float(m.group(5))}
+
+
+def cpu_baseline(iters: int = 1) -> dict:
+    """The reference's C++ matmul leg on the full 4096^2 workload when the host
+    is fast enough (probed at 1024^2), else on the largest size that fits in
+    about a minute; oracle port if the reference leg was not built."""
+    cores = host_cores()
+    if os.path.exists(cpp_mt_path()):
+        probe = run_cpp_mt(1024, 1, cores, timeout=120)
+        n = N_MM
+        # naive ijk slows with N (B's column walk leaves the caches): allow 3x
+        while n > 1024 and probe["ms"] * (n / 1024) ** 3 * 3 * iters > 60_000:
+            n //= 2
+        r = run_cpp_mt(n, iters, cores)
+        return {"value": r["tflops"], "unit": "TFLOP/s", "cores": r["threads"], "kind": "reference",
+                "sample": f"benches/matmul/cpp_mt.cpp f32 N={n}, {iters} iteration(s), min over "
+                          f"iterations, integer-generator inputs (timing is data-independent)",
+                "ms": r["ms"]}
+    import numpy as np
+    import oracle
+    rows = 64
+    A = oracle.gen(N_MM * N_MM, SEED_MM, 0)
+    B = oracle.gen(N_MM * N_MM, SEED_MM, N_MM * N_MM)
+    t0 = time.perf_counter()
+    oracle.matmul(A, B, N_MM, N_MM, N_MM, 0, rows, threads=cores)
+    dt = time.perf_counter() - t0
+    return {"value": 2.0 * rows * N_MM * N_MM / dt / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"oracle strict matmul, {rows} of 4096 rows"}
+
+
+def reference_arm(args) -> int:
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return 0
+    iters = max(1, min(args.steps, 3))
+    cb = cpu_baseline(iters)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": iters, "warmup": 0, "ms_per_step": cb.get("ms"),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "f32 matmul M=N=K=4096 (reference C++ CPU leg)"},
+        "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                                    "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---- our arm -----------------------------------------------------------------------------------
+
+class Dist:
+    def __init__(self, n_gpus: int):
+        self.world = env_int("WORLD_SIZE", 1)
+        self.rank = env_int("RANK", 0)
+        self.local = env_int("LOCAL_RANK", 0)
+        if self.world != n_gpus and not (self.world == 1 and n_gpus == 1):
+            raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={self.world}")
+        import torch
+        self.torch = torch
+        torch.cuda.set_device(self.local)
+        self.pg = None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", self.local))
+            self.dist = dist
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, v: float) -> float:
+        if self.world == 1:
+            return v
+        t = self.torch.tensor([v], dtype=self.torch.float64, device="cuda")
+        self.dist.all_reduce(t)
+        return float(t.item())
+
+    def bcast_bytes(self, b: bytes | None) -> bytes:
+        if self.world == 1:
+            return b
+        obj = [b]
+        self.dist.broadcast_object_list(obj, src=0)
+        return obj[0]
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+def run_ours(args) -> int:
+    d = Dist(args.gpus)
+    torch = d.torch
+    import flow_b200 as fb
+
+    nccl_id = d.bcast_bytes(fb.nccl_unique_id() if d.rank == 0 and d.world > 1 else None)
+    if d.world > 1:
+        ctx = fb.Context((d.local,), rank=d.rank, nranks=d.world, nccl_id=nccl_id, sync=False)
+    else:
+        ctx = fb.Context((d.local,), sync=False)
+    stream = torch.cuda.current_stream()
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def flush():
+        flush_buf.random_(0, 255)
+
+    mode = fb.TF32X3 if args.mode == "tf32x3" else fb.STRICT
+    n = N_MM
+    lo, hi = fb.shard_range(n, d.world, d.rank)
+    m = hi - lo
+    A = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    B = torch.empty(n * n, dtype=torch.float32, device="cuda")
+    C = torch.empty(max(m, 1) * n, dtype=torch.float32, device="cuda")
+    ctx.gen(A, SEED_MM, lo * n)
+    if d.rank == 0:
+        ctx.gen(B, SEED_MM, n * n)
+    else:
+        B.fill_(float("nan"))  # B arrives by broadcast inside every step
+    local_site = fb.matmul_site(m, n, n)
+    ctx.synchronize()
+
+    def step(ev0=None, ev1=None, ev2=None):
+        if ev0 is not None:
+            ev0.record(stream)
+        if d.world > 1:
+            ctx.broadcast([B], root=0)
+        if ev1 is not None:
+            ev1.record(stream)
+        ctx.matmul(local_site, A, B, C, mode)
+        if ev2 is not None:
+            ev2.record(stream)
+
+    for _ in range(args.warmup):
+        flush()
+        step()
+    ctx.synchronize()
+    torch.cuda.synchronize()
+
+    clocks = Clocks(smi_device(d.local))
+    clocks.start()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    d.barrier()
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        flush()
+        step(*evs[i])
+    ctx.synchronize()
+    torch.cuda.synchronize()
+    d.barrier()
+    clk = clocks.stop()
+    step_ms = [e[0].elapsed_time(e[2]) for e in evs]
+    kern_ms = [e[1].elapsed_time(e[2]) for e in evs]
+    ms = d.max(sum(step_ms) / len(step_ms))
+    kms = d.max(sum(kern_ms) / len(kern_ms))
+    flops = 2.0 * n ** 3
+    value = flops / (ms * 1e-3) / 1e12
+
+    # bit-exactness spot check of this run's output (strict mode): one row
+    # against the oracle is cheap; the full parity suite lives in tests/.
+    check = None
+    if mode == fb.STRICT and d.rank == 0 and m > 0 and args.check:
+        import numpy as np
+        import oracle
+        Ah = oracle.gen(n, SEED_MM, 0)
+        Bh = oracle.gen(n * n, SEED_MM, n * n)
+        want = oracle.matmul(Ah, Bh, 1, n, n)
+        got = C[:n].cpu().numpy()
+        check = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+
+    # e2e through the public API with host buffers: per step, pinned A block
+    # (and B on rank 0) H2D, the sharded site call, C block D2H.
+    e2e = None
+    if not args.no_e2e:
+        A_h = torch.empty(m * n, dtype=torch.float32, pin_memory=True)
+        B_h = torch.empty(n * n, dtype=torch.float32, pin_memory=True)
+        C_h = torch.empty(max(m, 1) * n, dtype=torch.float32, pin_memory=True)
+        A_h.copy_(A.cpu())
+        B_h.copy_(B.cpu())
+        e_steps = max(2, min(args.steps, 5))
+
+        def e2e_step():
+            A.copy_(A_h, non_blocking=True)
+            if d.rank == 0:
+                B.copy_(B_h, non_blocking=True)
+            if d.world > 1:
+                ctx.matmul_sharded(fb.matmul_site(n, n, n), [A], [B], [C], [m], root=0, mode=mode)
+            else:
+                ctx.matmul(local_site, A, B, C, mode)
+            C_h.copy_(C, non_blocking=True)
+
+        e2e_step()
+        ctx.synchronize()
+        torch.cuda.synchronize()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        d.barrier()
+        ev[0].record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        ev[1].record(stream)
+        ctx.synchronize()
+        torch.cuda.synchronize()
+        e_ms = d.max(ev[0].elapsed_time(ev[1]) / e_steps)
+        h2d = d.sum(float(m * n * 4 + (n * n * 4 if d.rank == 0 else 0)))
+        d2h = d.sum(float(m * n * 4))
+        e2e = {"value": flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": e_steps,
+               "path": "pinned host A,B -> mapal_gpu_matmul_f32[_sharded] -> pinned host C"}
+
+    pk = peaks()
+    sm_mhz = clk["sm_mhz"] if clk else pk["sm_max_mhz"]
+    sms = ctx.profile().sm_count
+    # strict: one FP32 op per lane per clock (a MAC is a rounded mul + a rounded add)
+    peak_max = sms * 128 * pk["sm_max_mhz"] * 1e6 / 1e12
+    per_rank_flops = 2.0 * m * n * n
+    achieved = per_rank_flops / (kms * 1e-3) / 1e12 if kms > 0 else None
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
+        t = json.load(open(tpath)).get("mm_strict_kernel" if mode == fb.STRICT else "mm_tf32x3")
+        if t and t.get("m") == m:
+            traffic = t.get("bytes")
+    roofline = {
+        "bound": "fp32" if mode == fb.STRICT else "tensor",
+        "kernel": "mm_strict_kernel" if mode == fb.STRICT else "mm_tf32x3",
+        "achieved": achieved, "unit": "TFLOP/s",
+        "peak": peak_max, "frac": achieved / peak_max if achieved else None,
+        "peak_basis": f"{sms} SMs x 128 FP32 lanes x {pk['sm_max_mhz']:.0f} MHz (max clock, "
+                      f"MEASURED_PEAKS sm_max_mhz), 1 op per lane per clock",
+        "frac_at_sampled_clock": (achieved / (sms * 128 * sm_mhz * 1e6 / 1e12)) if achieved else None,
+        "frac_of_ffma_peak": achieved / (2 * peak_max) if achieved else None,
+        "traffic": traffic, "per_launch_flops": per_rank_flops,
+    }
+
+    streaming = None
+    if not args.no_streaming:
+        streaming = run_streaming(ctx, d, fb, torch, flush, pk)
+
+    cb = None
+    if d.rank == 0 and d.world == 1 and not args.no_cpu:
+        try:
+            cb = cpu_baseline(1)
+        except Exception as e:  # the bench line still stands without it
+            cb = {"error": str(e)[:200]}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": d.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": value / BASELINE_TFLOPS,
+        "vs_baseline_ref": "reference rung-0 CUDA matmul N=4096 f32, 57.2 ms = 2.40 TFLOP/s on RTX 4090 "
+                           "(docs/performance/matmul/s23.md:18)",
+        "dtype": "f32", "data": "synthetic: A, B uniform[-1,1) from seed 2 (seeded i32-hash stream), on device",
+        "config": {"workload": f"f32 matmul site M=N=K=4096, {args.mode}"
+                               + (" (bit-exact with the interpreter)" if mode == fb.STRICT else ""),
+                   "M": n, "N": n, "K": n, "mode": args.mode,
+                   "parallelism": f"row-shard x{d.world}, B broadcast (NCCL) inside each step",
+                   "l2": "flushed between timed steps (256 MiB write)"},
+        "roofline": roofline, "cpu_baseline": cb, "e2e": e2e, "gpu_launches": args.steps,
+        "clocks": clk, "kernel_ms_per_step": kms, "strict_row_check": check,
+        "streaming": streaming,
+    }
+    if d.rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    d.close()
+    return 0
+
+
+def time_launches(torch, stream, fn, flush, reps: int) -> float:
+    """Mean device ms of fn over reps launches, L2 flushed before each."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+    fn()
+    for a, b in evs:
+        flush()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return sum(a.elapsed_time(b) for a, b in evs) / reps
+
+
+def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
+    stream = torch.cuda.current_stream()
+    hbm = pk["hbm_gbs"]
+    out = {"hbm_peak_gbs": hbm, "peak_source": pk["source"], "l2": "flushed before every launch"}
+    reps = 10
+
+    def rec(name, nbytes, ms, extra=None):
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        r = {"ms": ms, "bytes": nbytes, "gbs": gbs, "frac_hbm": gbs / hbm}
+        if extra:
+            r.update(extra)
+        out[name] = r
+
+    if d.world == 1:
+        n = 1 << 20
+        x = torch.empty(n, dtype=torch.float32, device="cuda")
+        y0 = torch.empty_like(x)
+        y = torch.empty_like(x)
+        ctx.gen(x, 1, 0)
+        ctx.gen(y0, 1, n)
+        rec("saxpy_2^20", 12 * n, time_launches(torch, stream, lambda: ctx.saxpy(2.5, x, y0, y), flush, reps))
+        side = 1024
+        tsite = fb.transpose_site(side, side)
+        rec("transpose_1024^2", 8 * side * side,
+            time_launches(torch, stream, lambda: ctx.transpose(tsite, x, y), flush, reps))
+        idx = torch.empty(n, dtype=torch.int32, device="cuda")
+        ctx.gen_index(idx, 1, n, n)
+        rec("gather_2^20", 12 * n, time_launches(torch, stream, lambda: ctx.gather(x, idx, y), flush, reps),
+            {"bytes_basis": "algorithmic 12 B/element"})
+        s = torch.empty(1, dtype=torch.float32, device="cuda")
+        xs = torch.empty(n, dtype=torch.float32, device="cuda")
+        ctx.gen(xs, 1, 0, fb.U01)
+        rec("sum_2^20", 4 * n, time_launches(torch, stream, lambda: ctx.fold_sum(xs, s), flush, reps))
+        taps = 64
+        n_out = n - taps + 1
+        w = torch.empty(taps, dtype=torch.float32, device="cuda")
+        ctx.gen(w, 1, n)
+        fsite = fb.fir_site(n_out, taps)
+        ms = time_launches(torch, stream, lambda: ctx.fir(fsite, w, x, y), flush, reps)
+        rec("fir_2^20x64", 4 * n + 4 * n_out + 4 * taps, ms,
+            {"flops": 2 * taps * n_out, "fp32_frac": 2 * taps * n_out / (ms * 1e-3) /
+             (ctx.profile().sm_count * 128 * pk["sm_max_mhz"] * 1e6)})
+        H = W = 1024
+        csite = fb.conv2d_site(H - 2, W - 2, W, H * W)
+        w9 = torch.empty(9, dtype=torch.float32, device="cuda")
+        ctx.gen(w9, 1, H * W)
+        rec("conv2d_1024^2_3x3", 4 * H * W + 4 * (H - 2) * (W - 2) + 36,
+            time_launches(torch, stream, lambda: ctx.conv2d_3x3(csite, w9, x, y), flush, reps))
+        del x, y0, y, idx, xs
+
+    # 2^30-class, sharded over the ranks (each rank its contiguous share).
+    big = {}
+    n = 1 << 30
+    lo, hi = fb.shard_range(n, d.world, d.rank)
+    m = hi - lo
+    x = torch.empty(m, dtype=torch.float32, device="cuda")
+    y0 = torch.empty_like(x)
+    y = torch.empty_like(x)
+    ctx.gen(x, 3, lo)
+    ctx.gen(y0, 3, n + lo)
+    ms = d.max(time_launches(torch, stream, lambda: ctx.saxpy_sharded(2.5, [x], [y0], [y]), lambda: None, 3))
+    big["saxpy_2^30"] = {"ms": ms, "gbs": 12 * n / (ms * 1e-3) / 1e9}
+    del y0, y
+    s = torch.empty(1, dtype=torch.float32, device="cuda")
+    ctx.gen(x, 3, lo, fb.U01)
+    ms = d.max(time_launches(torch, stream, lambda: ctx.fold_sum_sharded([x], [s]), lambda: None, 3))
+    big["sum_2^30"] = {"ms": ms, "gbs": 4 * n / (ms * 1e-3) / 1e9, "collective": "NCCL all-reduce f64"}
+    del x
+    ng = 1 << 28
+    lo, hi = fb.shard_range(ng, d.world, d.rank)
+    xg = torch.empty(ng, dtype=torch.float32, device="cuda")
+    if d.rank == 0:
+        ctx.gen(xg, 3, 0)
+    ctx.broadcast([xg], root=0)  # x replicated once, outside the timed region
+    idx = torch.empty(hi - lo, dtype=torch.int32, device="cuda")
+    ctx.gen_index(idx, 3, ng + lo, ng)
+    yg = torch.empty(hi - lo, dtype=torch.float32, device="cuda")
+    ms = d.max(time_launches(torch, stream, lambda: ctx.gather_sharded([xg], [idx], [yg]), lambda: None, 3))
+    big["gather_2^28"] = {"ms": ms, "gbs": 12 * ng / (ms * 1e-3) / 1e9,
+                          "bytes_basis": "algorithmic 12 B/element; x replicated by NCCL broadcast at setup"}
+    ctx.synchronize()
+    for k, v in big.items():
+        v["frac_hbm_per_gpu"] = v["gbs"] / d.world / hbm
+    out["sharded_2^30"] = big
+    return out
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--mode", choices=["strict", "tf32x3"], default="strict")
+    ap.add_argument("--no-streaming", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--check", action="store_true", help="bit-exact spot check of one output row")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+    if args.impl == "reference":
+        return reference_arm(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,118 @@
+// common.cuh — shared internals of libmapal_gpu (not part of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/mapal_gpu.h"
+
+// ---- NCCL, bound at run time ------------------------------------------------
+// The library never links libnccl: it dlopens libnccl.so.2 the first time a
+// multi-device context is created, so single-GPU users and CPU-only loads need
+// no NCCL. Only the handful of entry points below are used.
+typedef struct ncclComm* ncclComm_t;
+struct NcclId {
+  char internal[128];
+};
+enum NcclDtype { kNcclFloat32 = 7, kNcclFloat64 = 8 };
+enum NcclOp { kNcclSum = 0 };
+
+struct NcclApi {
+  bool loaded = false;
+  std::string error;
+  int (*GetUniqueId)(NcclId*) = nullptr;
+  int (*CommInitRank)(ncclComm_t*, int, NcclId, int) = nullptr;
+  int (*CommInitAll)(ncclComm_t*, int, const int*) = nullptr;
+  int (*CommDestroy)(ncclComm_t) = nullptr;
+  int (*AllReduce)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+  int (*Broadcast)(const void*, void*, size_t, int, int, ncclComm_t, cudaStream_t) = nullptr;
+  int (*GroupStart)() = nullptr;
+  int (*GroupEnd)() = nullptr;
+  const char* (*GetErrorString)(int) = nullptr;
+};
+NcclApi* nccl_api();  // loads on first use; check ->loaded
+
+// ---- context ------------------------------------------------------------------
+
+struct DeviceSlot {
+  int device = -1;
+  cudaStream_t stream = nullptr;      // the stream work is enqueued on
+  cudaStream_t own_stream = nullptr;  // created by the context
+  unsigned* trap = nullptr;           // device trap flag: 0 quiescent, kind+1 after a trap
+  unsigned* trap_host = nullptr;      // pinned readback slot
+  // Fold scratch: one f64 partial per block, a block-arrival counter and a
+  // f64 cell for cross-rank combination. Allocated once at context creation.
+  double* fold_partials = nullptr;
+  unsigned* fold_counter = nullptr;
+  double* fold_total = nullptr;
+  // Growable arena for the 3xTF32 operand splits (cudaMalloc on growth only).
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  ncclComm_t comm = nullptr;
+  MapalGpuProfile prof{};
+};
+
+struct MapalGpuCtx {
+  std::vector<DeviceSlot> dev;
+  int nranks = 1;  // ranks of the communicator
+  int rank0 = 0;   // global rank of local device 0
+  bool sync = true;
+};
+
+// Blocks per fold launch is fixed per n (deterministic); this bounds it.
+constexpr int kFoldMaxBlocks = 4 * 148 * 4;
+
+// ---- error plumbing -------------------------------------------------------------
+int set_error(int code, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what);
+#define MAPAL_CUDA(call)                                   \
+  do {                                                     \
+    cudaError_t _e = (call);                               \
+    if (_e != cudaSuccess) return cuda_fail(_e, #call);    \
+  } while (0)
+#define MAPAL_TRY(expr)          \
+  do {                           \
+    int _rc = (expr);            \
+    if (_rc != 0) return _rc;    \
+  } while (0)
+
+// Validate ctx and local index; make the device current.
+int enter(MapalGpuCtx* ctx, int local = 0);
+// After a launch: report launch errors; in sync mode wait and decode traps.
+int finish(MapalGpuCtx* ctx, int local, bool trap_capable);
+// Wait and decode the trap flag of one device.
+int drain(DeviceSlot& d);
+// Ensure the arena of a device holds `bytes` (grows, never shrinks).
+int arena_reserve(DeviceSlot& d, size_t bytes);
+
+// Grid size for a streaming kernel: enough resident blocks to fill every SM.
+inline unsigned stream_grid(uint64_t work_items, int threads, int sms, int blocks_per_sm) {
+  uint64_t want = (work_items + threads - 1) / threads;
+  uint64_t cap = (uint64_t)sms * blocks_per_sm;
+  if (want > cap) want = cap;
+  if (want == 0) want = 1;
+  return (unsigned)want;
+}
+
+inline bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+// ---- site-class launchers (one per .cu file) -----------------------------------
+int launch_fill(cudaStream_t s, int sms, float* out, float v, uint64_t n);
+int launch_gen_affine(cudaStream_t s, int sms, float* out, uint64_t n, int64_t start, int32_t mul,
+                      int32_t add, int32_t mod, int32_t sub);
+int launch_gen_f32(cudaStream_t s, int sms, float* out, uint64_t n, int32_t seed, int64_t offset,
+                   int kind);
+int launch_saxpy(cudaStream_t s, int sms, float a, const float* x, const float* y0, float* y,
+                 uint64_t n);
+int launch_gather(cudaStream_t s, int sms, const float* x, uint64_t n_x, const int32_t* idx,
+                  float* out, uint64_t n, unsigned* trap);
+int launch_fold_sum(cudaStream_t s, int sms, const float* x, uint64_t n, float seed, double* partials,
+                    unsigned* counter, float* out_f32, double* out_f64);
+int launch_finalize_sum(cudaStream_t s, const double* total, float seed, float* out);
+int launch_matmul_strict(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
+                         uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed);
+int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C, uint64_t M,
+                         uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed);

@@ -1,0 +1,125 @@
+// reduce.cu — the sum fold `(seed, x) -> fold { acc, v -> acc + v }`
+// (benches/shapes/reduce_1048576.mapal:10).
+//
+// The reference runs every top-level fold as one device thread
+// (<<<1,1>>>, crates/backends/cuda/src/kernel.rs:1484-1642; DESIGN BC4),
+// because an f32 left fold is only bit-exact in sequence (ADR-0028 keeps f32
+// folds sequential-pinned). This site is the one place the library trades
+// bit-exactness for parallelism, under a stated tolerance: one launch, every
+// SM streaming 128-bit loads, each thread summing its elements in f64, a
+// fixed warp-shuffle + block tree, and the last block to finish combining the
+// per-block partials in a fixed order. The shape of the tree depends only on
+// n and the SM count, so the result is the same on every run.
+#include "common.cuh"
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+
+__device__ __forceinline__ double block_sum(double v, double* smem) {
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // smem may still be read by a previous call
+  if (lane == 0) smem[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (threadIdx.x == 0)
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t += smem[w];
+  return t;  // valid in thread 0
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(kThreads) fold_sum_kernel(const float* __restrict__ x, uint64_t n,
+                                                            float seed, double* partials,
+                                                            unsigned* counter, float* out_f32,
+                                                            double* out_f64) {
+  __shared__ double smem[kWarps];
+  __shared__ bool last;
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  const uint64_t gid = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  double acc = 0.0;
+  uint64_t tail = 0;
+  if (kVec) {
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    const uint64_t n4 = n / 4;
+    uint64_t i = gid;
+    for (; i + stride < n4; i += 2 * stride) {
+      float4 a = __ldcs(x4 + i), b = __ldcs(x4 + i + stride);
+      acc += (double)a.x;
+      acc += (double)a.y;
+      acc += (double)a.z;
+      acc += (double)a.w;
+      acc += (double)b.x;
+      acc += (double)b.y;
+      acc += (double)b.z;
+      acc += (double)b.w;
+    }
+    if (i < n4) {
+      float4 a = __ldcs(x4 + i);
+      acc += (double)a.x;
+      acc += (double)a.y;
+      acc += (double)a.z;
+      acc += (double)a.w;
+    }
+    tail = n4 * 4;
+  }
+  for (uint64_t i = tail + gid; i < n; i += stride) acc += (double)__ldcs(x + i);
+
+  double bsum = block_sum(acc, smem);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = bsum;
+    __threadfence();
+    unsigned ticket = atomicAdd(counter, 1u);
+    last = ticket == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  // Last block: combine the partials in block order (fixed).
+  __threadfence();
+  double t = 0.0;
+  for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) t += __ldcg(partials + b);
+  double total = block_sum(t, smem);
+  if (threadIdx.x == 0) {
+    if (out_f64) *out_f64 = total;
+    if (out_f32) *out_f32 = (float)((double)seed + total);
+    *counter = 0u;  // ready for the next launch on this stream
+  }
+}
+
+__global__ void finalize_sum_kernel(const double* total, float seed, float* out) {
+  *out = (float)((double)seed + *total);
+}
+
+}  // namespace
+
+int launch_fold_sum(cudaStream_t s, int sms, const float* x, uint64_t n, float seed, double* partials,
+                    unsigned* counter, float* out_f32, double* out_f64) {
+  uint64_t want = (n + (uint64_t)kThreads * 8 - 1) / ((uint64_t)kThreads * 8);
+  uint64_t cap = (uint64_t)sms * 4;
+  if (cap > (uint64_t)kFoldMaxBlocks) cap = kFoldMaxBlocks;
+  unsigned grid = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
+  if (n >= 4 && aligned16(x))
+    fold_sum_kernel<true><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64);
+  else
+    fold_sum_kernel<false><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64);
+  return 0;
+}
+
+int launch_finalize_sum(cudaStream_t s, const double* total, float seed, float* out) {
+  finalize_sum_kernel<<<1, 1, 0, s>>>(total, seed, out);
+  return 0;
+}
+
+extern "C" int mapal_gpu_fold_sum_f32(MapalGpuCtx* ctx, float seed, const float* x, uint64_t n,
+                                      float* out) {
+  MAPAL_TRY(enter(ctx));
+  if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
+  if (n && !x) return set_error(MAPAL_ERR_INVALID, "x is null");
+  DeviceSlot& d = ctx->dev[0];
+  MAPAL_TRY(launch_fold_sum(d.stream, d.prof.sm_count, x, n, seed, d.fold_partials, d.fold_counter,
+                            out, nullptr));
+  return finish(ctx, 0, false);
+}

@@ -1,0 +1,119 @@
+// sharded.cu — the auto-partitioner's multi-GPU sites.
+//
+// The reference is one process with no multi-GPU path. Its bulk sites split
+// naturally, and only where they do does this library shard them:
+//  * saxpy: contiguous equal shards, no exchange;
+//  * sum:   contiguous shards, one f64 partial per rank, one NCCL all-reduce;
+//  * gather: idx sharded, x replicated (NCCL broadcast, done once by the caller);
+//  * matmul: A row blocks, B replicated by NCCL broadcast, C row blocks stay put.
+// A context spans either several devices of one process (arrays hold one
+// pointer per local device) or one device of a multi-process job (arrays of
+// length 1); the collectives run over the context's communicator either way.
+#include "common.cuh"
+
+int nccl_allreduce_f64(MapalGpuCtx* ctx, double* const* buf, size_t count);
+int nccl_broadcast_f32(MapalGpuCtx* ctx, float* const* buf, size_t count, int root);
+int tile_site_on(MapalGpuCtx* ctx, int local, const MapalTileSite* site, const float* a, const float* b,
+                 float* out, int mode);
+
+namespace {
+
+// Finish a multi-device call: launch errors, then (sync mode) every device's
+// completion and trap flag. The first nonzero status wins.
+int finish_all(MapalGpuCtx* ctx, bool trap_capable) {
+  int first = 0;
+  for (int i = 0; i < (int)ctx->dev.size(); ++i) {
+    int rc = enter(ctx, i);
+    if (!rc) rc = finish(ctx, i, trap_capable);
+    if (rc && !first) first = rc;
+  }
+  return first;
+}
+
+int check_arrays(MapalGpuCtx* ctx, const void* a, const void* b, const void* c) {
+  if (!ctx) return set_error(MAPAL_ERR_INVALID, "ctx is null");
+  if (!a || !b || !c) return set_error(MAPAL_ERR_INVALID, "null pointer array");
+  return 0;
+}
+
+}  // namespace
+
+extern "C" int mapal_gpu_saxpy_sharded(MapalGpuCtx* ctx, float a, const float* const* x,
+                                       const float* const* y0, float* const* y, const uint64_t* n) {
+  MAPAL_TRY(check_arrays(ctx, x, y0, y));
+  if (!n) return set_error(MAPAL_ERR_INVALID, "n is null");
+  for (int i = 0; i < (int)ctx->dev.size(); ++i) {
+    MAPAL_TRY(enter(ctx, i));
+    if (n[i] && (!x[i] || !y0[i] || !y[i])) return set_error(MAPAL_ERR_INVALID, "null shard");
+    DeviceSlot& d = ctx->dev[i];
+    MAPAL_TRY(launch_saxpy(d.stream, d.prof.sm_count, a, x[i], y0[i], y[i], n[i]));
+  }
+  return finish_all(ctx, false);
+}
+
+extern "C" int mapal_gpu_fold_sum_f32_sharded(MapalGpuCtx* ctx, float seed, const float* const* x,
+                                              const uint64_t* n, float* const* out) {
+  MAPAL_TRY(check_arrays(ctx, x, n, out));
+  std::vector<double*> totals(ctx->dev.size());
+  for (int i = 0; i < (int)ctx->dev.size(); ++i) {
+    MAPAL_TRY(enter(ctx, i));
+    if ((n[i] && !x[i]) || !out[i]) return set_error(MAPAL_ERR_INVALID, "null shard");
+    DeviceSlot& d = ctx->dev[i];
+    totals[i] = d.fold_total;
+    MAPAL_TRY(launch_fold_sum(d.stream, d.prof.sm_count, x[i], n[i], 0.0f, d.fold_partials,
+                              d.fold_counter, nullptr, d.fold_total));
+  }
+  MAPAL_TRY(nccl_allreduce_f64(ctx, totals.data(), 1));
+  for (int i = 0; i < (int)ctx->dev.size(); ++i) {
+    MAPAL_TRY(enter(ctx, i));
+    MAPAL_TRY(launch_finalize_sum(ctx->dev[i].stream, ctx->dev[i].fold_total, seed, out[i]));
+  }
+  return finish_all(ctx, false);
+}
+
+extern "C" int mapal_gpu_broadcast_f32(MapalGpuCtx* ctx, float* const* buf, uint64_t n, int root) {
+  if (!ctx || !buf) return set_error(MAPAL_ERR_INVALID, "null argument");
+  if (root < 0 || root >= ctx->nranks) return set_error(MAPAL_ERR_INVALID, "root out of range");
+  if (n == 0) return 0;
+  for (int i = 0; i < (int)ctx->dev.size(); ++i)
+    if (!buf[i]) return set_error(MAPAL_ERR_INVALID, "null buffer");
+  MAPAL_TRY(nccl_broadcast_f32(ctx, buf, n, root));
+  return finish_all(ctx, false);
+}
+
+extern "C" int mapal_gpu_gather_sharded(MapalGpuCtx* ctx, const float* const* x, uint64_t n_x,
+                                        const int32_t* const* idx, float* const* out, const uint64_t* n) {
+  MAPAL_TRY(check_arrays(ctx, x, idx, out));
+  if (!n) return set_error(MAPAL_ERR_INVALID, "n is null");
+  for (int i = 0; i < (int)ctx->dev.size(); ++i) {
+    MAPAL_TRY(enter(ctx, i));
+    if (n[i] && (!idx[i] || !out[i] || (n_x && !x[i]))) return set_error(MAPAL_ERR_INVALID, "null shard");
+    DeviceSlot& d = ctx->dev[i];
+    MAPAL_TRY(launch_gather(d.stream, d.prof.sm_count, x[i], n_x, idx[i], out[i], n[i], d.trap));
+  }
+  return finish_all(ctx, true);
+}
+
+extern "C" int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSite* site,
+                                            const float* const* A, float* const* B, float* const* C,
+                                            const uint64_t* m, int root, int mode) {
+  MAPAL_TRY(check_arrays(ctx, A, B, C));
+  if (!site || !m) return set_error(MAPAL_ERR_INVALID, "null argument");
+  if (mode != MAPAL_MATMUL_STRICT && mode != MAPAL_MATMUL_TF32X3)
+    return set_error(MAPAL_ERR_INVALID, "unknown matmul mode");
+  if (root < 0 || root >= ctx->nranks) return set_error(MAPAL_ERR_INVALID, "root out of range");
+  // B is replicated first: every rank's full B buffer receives root's.
+  const uint64_t b_elems = site->b.len;
+  MAPAL_TRY(nccl_broadcast_f32(ctx, B, b_elems, root));
+  for (int i = 0; i < (int)ctx->dev.size(); ++i) {
+    MAPAL_TRY(enter(ctx, i));
+    // The device's site: its own row block (A[i] points at the block's first
+    // row), the same columns, k order and B record.
+    MapalTileSite local = *site;
+    local.rows = m[i];
+    local.a.base = 0;
+    local.a.len = m[i] ? (m[i] - 1) * site->a.ci + site->k : 0;
+    MAPAL_TRY(tile_site_on(ctx, i, &local, A[i], B[i], C[i], mode));
+  }
+  return finish_all(ctx, false);
+}

@@ -1,0 +1,330 @@
+/*
+ * mapal_gpu.h — C ABI of libmapal_gpu, the sm_100a (B200) runtime for Mapal's
+ * bulk array sites.
+ *
+ * What this replaces. The reference compiles each bulk site of a sealed
+ * CategoryIr into its own `__global__` function and launches it from emitted
+ * host code:
+ *   - `emit` / `emit_with_opts` produce one .cu translation unit
+ *     (crates/backends/cuda/src/lib.rs:72-111);
+ *   - each site becomes a kernel from the emitters in
+ *     crates/backends/cuda/src/kernel.rs:1156-1642;
+ *   - emitted host glue launches it and checks the trap flag
+ *     (crates/backends/cuda/src/func.rs:1159-1197, module.rs:61-95).
+ * Here the kernels are fixed, hand-written sm_100a kernels. A backend calls
+ * one entry point per recognized site class, passing the site's record
+ * (TileSite, crates/mapal-ir/src/algo.rs:335-345; MoveSite, algo.rs:309-333)
+ * and caller-owned device buffers. No C++ type crosses this boundary.
+ *
+ * Status protocol (every entry point returns int):
+ *    0  ok
+ *    1  trap div_zero   } the device trap-flag decode of module.rs:86-94:
+ *    2  trap index_oob  } flag = kind + 1, host maps to exit 101
+ *   <0  infrastructure error (the reference's exit-102 class, module.rs:66-71);
+ *       mapal_gpu_last_error() returns the message.
+ *
+ * Threading: one host thread per context. Calls are stream-ordered on the
+ * context's stream for the device. With sync mode on (the default) a call
+ * returns after its work finished and any trap has been decoded, which is the
+ * reference's launch-then-check order. With sync mode off a call returns
+ * after enqueueing, and traps surface at mapal_gpu_synchronize().
+ *
+ * Floating point: every f32 `+` and `*` of a site is separately rounded
+ * (round-to-nearest-even, no contraction, denormals kept), as the
+ * interpreter evaluates them (crates/mapal-interp/src/eval.rs:572-585).
+ * Exceptions, each stated where it applies: fold sums reassociate
+ * (mapal_gpu_fold_sum_f32) and MAPAL_MATMUL_TF32X3 uses tensor cores.
+ */
+#ifndef MAPAL_GPU_H
+#define MAPAL_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Every symbol declared here is exported even when the library is built with
+ * hidden default visibility. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+#define MAPAL_GPU_ABI_VERSION 1
+
+/* ---- status codes ------------------------------------------------------ */
+#define MAPAL_OK 0
+#define MAPAL_TRAP_DIV_ZERO 1  /* mapal_trap(0) in mapal-rt/src/lib.rs:71-81 */
+#define MAPAL_TRAP_INDEX_OOB 2 /* mapal_trap(1) */
+#define MAPAL_ERR_INVALID (-1)     /* bad argument or descriptor */
+#define MAPAL_ERR_UNSUPPORTED (-2) /* site shape this library has no kernel for
+                                      (EmitError::Unsupported, cuda/src/lib.rs:74-80) */
+#define MAPAL_ERR_CUDA (-3)        /* CUDA runtime / driver error */
+#define MAPAL_ERR_NCCL (-4)        /* NCCL error or NCCL unavailable */
+#define MAPAL_ERR_NOMEM (-5)       /* device allocation of internal scratch failed */
+#define MAPAL_ERR_TIMEOUT (-6)     /* a bounded device wait gave up */
+
+/* ---- records ------------------------------------------------------------ */
+
+/* The `k = kq*div + kr` decomposition of a fold axis (TileKSplit,
+ * crates/mapal-ir/src/algo.rs:245-257). div == 0 means "no split". */
+typedef struct MapalKSplit {
+  uint64_t div;
+  uint64_t cq; /* address coefficient on k / div */
+  uint64_t cr; /* address coefficient on k % div */
+} MapalKSplit;
+
+/* One affine array read of a tiled site (TileRead, algo.rs:227-240):
+ *   addr(i, lane, k) = base + ci*i + clane*lane + ck*k
+ *                      + ksplit.cq*(k/div) + ksplit.cr*(k%div)
+ * `len` is the read array's length in elements; reads at addr >= len trap
+ * index_oob, as the interpreter's Index does (eval.rs:655-669). */
+typedef struct MapalTileRead {
+  uint64_t base;
+  uint64_t ci;
+  uint64_t ck;
+  uint64_t clane;
+  MapalKSplit ksplit;
+  uint64_t len;
+} MapalTileRead;
+
+/* A recognized map-of-fold site (TileSite, algo.rs:335-345). The site
+ * computes rows*c cells, cell t = i*c + lane (i = t / c, lane = t % c):
+ *   acc = seed
+ *   for k in 0..k:  p   = mul_a_first ? a[addr_a] * b[addr_b] : b[addr_b] * a[addr_a]
+ *                   acc = add_acc_first ? acc + p : p + acc
+ *   out[t] = acc
+ * with the fold strictly left to right (eval.rs:326-359). */
+typedef struct MapalTileSite {
+  uint64_t rows;
+  uint64_t c;
+  uint64_t k;
+  MapalTileRead a;
+  MapalTileRead b;
+  float seed;
+  uint8_t mul_a_first;
+  uint8_t add_acc_first;
+  uint8_t reserved[2];
+} MapalTileSite;
+
+/* A fold-less move site (MoveSite, algo.rs:309-333): the map over
+ * t in [0, rows*width) computes out[t] = in[cq*(t/width) + cr*(t%width)].
+ * A transpose of an R x C row-major matrix is width=R, rows=C, cq=1, cr=C. */
+typedef struct MapalMoveSite {
+  uint64_t width;
+  uint64_t rows;
+  uint64_t cq;
+  uint64_t cr;
+  uint64_t len; /* length of `in` in elements */
+} MapalMoveSite;
+
+/* Machine facts for the tiler: the sm_100a counterpart of the reference's
+ * placeholder Machine::Gpu / CUDA_ADA profile
+ * (crates/backends/llvm/src/profile.rs:99-156, 781-800). */
+typedef struct MapalGpuProfile {
+  int32_t device;
+  int32_t cc_major;
+  int32_t cc_minor;
+  int32_t sm_count;
+  int32_t warp_size;
+  int32_t max_threads_per_block;
+  int32_t max_threads_per_sm;
+  int32_t regs_per_sm;
+  int64_t smem_per_sm;          /* bytes */
+  int64_t smem_per_block_optin; /* bytes, the opt-in maximum */
+  int64_t l2_bytes;
+  int64_t tmem_bytes_per_sm;    /* tensor memory: 128 lanes x 512 columns x 4 B */
+  int64_t hbm_bytes;
+  int32_t sm_clock_khz;         /* maximum SM clock */
+  int32_t mem_clock_khz;
+  int32_t mem_bus_bits;
+  int32_t cluster_launch;       /* 1 if thread-block clusters are supported */
+  char name[96];
+} MapalGpuProfile;
+
+/* matmul precision modes */
+#define MAPAL_MATMUL_STRICT 0 /* SIMT, separately rounded mul and add in the
+                                 interpreter's order: bit-identical */
+#define MAPAL_MATMUL_TF32X3 1 /* tcgen05 tensor cores, 3xTF32 split; opt-in,
+                                 within a stated relative error (ADR-0032's
+                                 tf32-class contract) */
+
+/* generator kinds for mapal_gpu_gen_f32 */
+#define MAPAL_GEN_U11 0 /* uniform[-1,1) */
+#define MAPAL_GEN_U01 1 /* uniform[0,1) */
+
+typedef struct MapalGpuCtx MapalGpuCtx;
+
+/* ---- lifecycle ------------------------------------------------------------ */
+
+/* Library ABI version (MAPAL_GPU_ABI_VERSION). */
+int mapal_gpu_abi_version(void);
+
+/* Message of the last error on this thread ("" if none). */
+const char* mapal_gpu_last_error(void);
+
+/* Number of visible CUDA devices (0 when no driver or no device). */
+int mapal_gpu_device_count(int* count);
+
+/* Create a context over the devices whose bits are set in device_mask (bit d =
+ * CUDA device d). Owns one stream per device, the device trap flags and, for
+ * more than one device, one NCCL communicator per device (single-process
+ * multi-GPU: the auto-partitioner's shape). Replaces the per-process
+ * trap_init() of the emitted prelude (module.rs:74-77). */
+int mapal_gpu_ctx_create(uint32_t device_mask, MapalGpuCtx** out);
+
+/* Create a context for one rank of a multi-process job (one process per GPU).
+ * All ranks pass the same 128-byte id, made once by
+ * mapal_gpu_nccl_unique_id() on one rank and shared by the caller. */
+int mapal_gpu_nccl_unique_id(uint8_t id[128]);
+int mapal_gpu_ctx_create_rank(int device, int nranks, int rank, const uint8_t id[128],
+                              MapalGpuCtx** out);
+
+int mapal_gpu_ctx_destroy(MapalGpuCtx* ctx);
+
+/* Number of devices this context drives in this process. */
+int mapal_gpu_ctx_local_devices(MapalGpuCtx* ctx, int* n);
+/* Total ranks of the context's communicator (1 for a one-device context). */
+int mapal_gpu_ctx_world(MapalGpuCtx* ctx, int* nranks, int* rank);
+
+/* Machine facts of local device `local`. */
+int mapal_gpu_profile(MapalGpuCtx* ctx, int local, MapalGpuProfile* out);
+
+/* Stream of local device `local` (a cudaStream_t). Replace it with a caller
+ * stream to order this library's work with the caller's. */
+int mapal_gpu_get_stream(MapalGpuCtx* ctx, int local, void** stream);
+int mapal_gpu_set_stream(MapalGpuCtx* ctx, int local, void* stream);
+
+/* 1 (default): calls return after completion with traps decoded.
+ * 0: calls return after enqueueing; traps surface at mapal_gpu_synchronize. */
+int mapal_gpu_set_sync(MapalGpuCtx* ctx, int sync);
+
+/* Wait for all work of the context; decode and clear the trap flags. */
+int mapal_gpu_synchronize(MapalGpuCtx* ctx);
+
+/* ---- input generators (iota / fill / widen and the seeded stream) ------- */
+/* The reference's Iota, Fill and Widen kernels (kernel.rs:1335-1378;
+ * eval.rs:238-248, 402-427), plus fused generators that recompute an element
+ * from its index the way elem_plan lets a consumer do (algo.rs:434-512). */
+
+/* out[i] = i for i < n (n <= 2^31) */
+int mapal_gpu_iota_i32(MapalGpuCtx* ctx, int32_t* out, uint64_t n);
+/* out[i] = v */
+int mapal_gpu_fill_f32(MapalGpuCtx* ctx, float* out, float v, uint64_t n);
+/* out[i] = (float)in[i]  (Widen i32 -> f32, round to nearest) */
+int mapal_gpu_widen_i32_f32(MapalGpuCtx* ctx, const int32_t* in, float* out, uint64_t n);
+/* out[i] = widen_f32((t*mul + add) % mod - sub), t = start + i, i32 wrapping
+ * arithmetic: the integer generators of the benches/shapes sources, fused. */
+int mapal_gpu_gen_affine_f32(MapalGpuCtx* ctx, float* out, uint64_t n, int64_t start,
+                             int32_t mul, int32_t add, int32_t mod, int32_t sub);
+/* out[i] = element (offset + i) of the seeded uniform stream `seed`
+ * (kind MAPAL_GEN_U11 or MAPAL_GEN_U01). */
+int mapal_gpu_gen_f32(MapalGpuCtx* ctx, float* out, uint64_t n, int32_t seed, int64_t offset,
+                      int kind);
+/* out[i] = index draw (offset + i) of stream `seed`, uniform in [0, range). */
+int mapal_gpu_gen_index_i32(MapalGpuCtx* ctx, int32_t* out, uint64_t n, int32_t seed,
+                            int64_t offset, int32_t range);
+
+/* ---- site classes ---------------------------------------------------------- */
+
+/* saxpy: y[i] = a*x[i] + y0[i] (benches/shapes/saxpy_1048576.mapal:11; the zip
+ * then map of kernel.rs:1249-1293 and 1156-1247, fused: 12 bytes/element).
+ * y may alias y0. */
+int mapal_gpu_map_saxpy(MapalGpuCtx* ctx, float a, const float* x, const float* y0, float* y,
+                        uint64_t n);
+
+/* Elementwise zip-map out[i] = x[i] OP y[i] for the float binary ops of
+ * eval.rs:572-585 (ADD, SUB, MUL, DIV, MOD = fmodf, as Rust's `%`). */
+#define MAPAL_OP_ADD 0
+#define MAPAL_OP_SUB 1
+#define MAPAL_OP_MUL 2
+#define MAPAL_OP_DIV 3
+#define MAPAL_OP_MOD 4
+int mapal_gpu_zip_map_f32(MapalGpuCtx* ctx, int op, const float* x, const float* y, float* out,
+                          uint64_t n);
+
+/* Move site (transpose and other affine permutations),
+ * benches/shapes/transpose_1024.mapal:11; MoveSite algo.rs:309-333. */
+int mapal_gpu_transpose(MapalGpuCtx* ctx, const MapalMoveSite* site, const float* in,
+                        float* out);
+
+/* Gather out[i] = x[idx[i]] with the Index bounds rule (eval.rs:655-669;
+ * kernel.rs:2655-2663): any idx outside [0, n_x) returns MAPAL_TRAP_INDEX_OOB
+ * (out is then unspecified), as the emitted guard stores kind+1 = 2. */
+int mapal_gpu_gather(MapalGpuCtx* ctx, const float* x, uint64_t n_x, const int32_t* idx,
+                     float* out, uint64_t n);
+
+/* Sum fold out = seed + x[0] + ... + x[n-1] (benches/shapes/reduce_1048576.mapal:10).
+ * out is a device pointer to one float. NOT bit-exact with the interpreter's
+ * left fold (ADR-0028 pins f32 folds sequential): this is a fixed-shape tree,
+ * accumulated in f64 and rounded once, so it is deterministic run to run and
+ * within 1e-6 * sum|x| of the exact sum. */
+int mapal_gpu_fold_sum_f32(MapalGpuCtx* ctx, float seed, const float* x, uint64_t n, float* out);
+
+/* FIR / window site (benches/shapes/fir_1048576.mapal:10-12):
+ * site must be rows=1, a = taps {ck=1, ci=0, clane=0}, b = signal {ck=1, clane=1,
+ * ci=0}: out[t] = fold_k(acc + w[k]*x[t+k]) from seed, k ascending. Bit-exact. */
+int mapal_gpu_fir_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* w,
+                      const float* x, float* out);
+
+/* 3x3 conv2d site (benches/shapes/conv2d_1024.mapal:11-15): a = 9 taps {ck=1},
+ * b = image {ci=stride, clane=1, ck=0, ksplit={3, stride, 1}}. Bit-exact. */
+int mapal_gpu_conv2d_3x3_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* w,
+                             const float* img, float* out);
+
+/* matmul site (benches/matmul/matmul1024_cap_f32.mapal:7-11): rows=M, c=N, k=K,
+ * a = A {ci=lda, ck=1, clane=0}, b = B {ci=0, ck=ldb, clane=1}, out row-major M x N.
+ * mode MAPAL_MATMUL_STRICT is bit-identical with the interpreter;
+ * MAPAL_MATMUL_TF32X3 is within max|C - C_ref| <= 1e-5 * ||A_i,:|| * ||B_:,j||. */
+int mapal_gpu_matmul_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* A,
+                         const float* B, float* C, int mode);
+
+/* Any TileSite: dispatches to the matmul, FIR or conv2d kernel when the record
+ * has that shape, else runs the generic one-thread-per-cell site kernel
+ * (bit-exact, the rung-0 shape). mode applies to matmul-shaped sites. */
+int mapal_gpu_tile_site_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* a,
+                            const float* b, float* out, int mode);
+
+/* ---- sharded sites (one pointer per local device, in local-device order) ----
+ * Partitioning is contiguous and equal up to one unit (mapal_gpu_shard_range).
+ * In a multi-process context each process passes arrays of length 1. */
+
+/* Range [lo, hi) of `n` units owned by global rank r of `nranks`. */
+int mapal_gpu_shard_range(uint64_t n, int nranks, int r, uint64_t* lo, uint64_t* hi);
+
+/* saxpy over contiguous shards; n[d] elements on local device d. No collective. */
+int mapal_gpu_saxpy_sharded(MapalGpuCtx* ctx, float a, const float* const* x,
+                            const float* const* y0, float* const* y, const uint64_t* n);
+
+/* Sum over contiguous shards: one f64 partial per rank, combined by an NCCL
+ * all-reduce; every local device receives the f32 result in out[d]. */
+int mapal_gpu_fold_sum_f32_sharded(MapalGpuCtx* ctx, float seed, const float* const* x,
+                                   const uint64_t* n, float* const* out);
+
+/* Broadcast n floats from global rank `root` into buf[d] on every device. */
+int mapal_gpu_broadcast_f32(MapalGpuCtx* ctx, float* const* buf, uint64_t n, int root);
+
+/* Gather with idx sharded and x replicated: x[d] holds n_x floats on every
+ * device (replicate it first with mapal_gpu_broadcast_f32). */
+int mapal_gpu_gather_sharded(MapalGpuCtx* ctx, const float* const* x, uint64_t n_x,
+                             const int32_t* const* idx, float* const* out, const uint64_t* n);
+
+/* Row-block matmul: device d holds its row block A[d] (m[d] rows x K) and a
+ * full B buffer B[d]; B on global rank `root` is broadcast to all B[d] first
+ * (NCCL), then each device computes C[d] = A[d] * B. site describes the full
+ * problem (rows = total M). Strict mode stays bit-exact: each cell's k order
+ * is untouched by the row split. */
+int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSite* site,
+                                 const float* const* A, float* const* B, float* const* C,
+                                 const uint64_t* m, int root, int mode);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MAPAL_GPU_H */

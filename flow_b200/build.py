@@ -25,8 +25,10 @@ INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB = os.path.join(HERE, "libmapal_gpu.so")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# -fmad=false: no multiply and add is ever contracted into an FMA (the
+# interpreter rounds each separately); it covers the packed f32x2 forms too.
 NVCC_FLAGS = ARCH + [
-    "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+    "-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC",
     "-Xcompiler", "-fvisibility=hidden", "-Xptxas", "-warn-spills", "-I", INCLUDE,
 ]
 CXX_FLAGS = ["-O2", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-ffp-contract=off", "-I", INCLUDE]
@@ -64,6 +66,13 @@ def _compile(src: str, force: bool, hdr_mtime: float) -> str:
 
 def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(BUILD, exist_ok=True)
+    # A change of compiler flags invalidates every object.
+    stamp = os.path.join(BUILD, "flags.txt")
+    flags = " ".join(NVCC_FLAGS + CXX_FLAGS)
+    if not os.path.exists(stamp) or open(stamp).read() != flags:
+        force = True
+        with open(stamp, "w") as f:
+            f.write(flags)
     srcs = sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
     hdr = _headers_mtime()
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:

@@ -285,8 +285,10 @@ extern "C" int mapal_gpu_get_stream(MapalGpuCtx* ctx, int local, void** stream) 
 
 extern "C" int mapal_gpu_set_stream(MapalGpuCtx* ctx, int local, void* stream) {
   MAPAL_TRY(enter(ctx, local));
-  DeviceSlot& d = ctx->dev[local];
-  d.stream = stream ? (cudaStream_t)stream : d.own_stream;
+  // Taken as given, as everywhere in CUDA: NULL is the legacy default stream.
+  // The context's own stream is the value mapal_gpu_get_stream returned
+  // before any set_stream.
+  ctx->dev[local].stream = (cudaStream_t)stream;
   return 0;
 }
 
@@ -318,6 +320,7 @@ int drain(DeviceSlot& d) {
     MAPAL_CUDA(cudaStreamSynchronize(d.stream));
     if (kind == 1) return set_error(MAPAL_TRAP_DIV_ZERO, "mapal trap: div_zero");
     if (kind == 2) return set_error(MAPAL_TRAP_INDEX_OOB, "mapal trap: index_oob");
+    if (kind & 0x100u) return set_error(MAPAL_ERR_TIMEOUT, "a bounded device wait gave up (tensor-core pipeline)");
     return set_error(MAPAL_ERR_CUDA, "trap flag holds an unknown kind");
   }
   return 0;

@@ -1,9 +1,406 @@
-// matmul_tf32x3.cu — opt-in tensor-core matmul (3xTF32 on tcgen05); see below.
+// matmul_tf32x3.cu — the opt-in tensor-core matmul: 3xTF32 on tcgen05.
+//
+// ADR-0032 (docs/decisions/ADR-0032-precision-contracts-vs-backend-config.md)
+// puts a `tf32-class` precision contract beside `exact`: a matmul site may
+// be evaluated on tensor cores when the program opts in, within a stated
+// error. This is that path (MAPAL_MATMUL_TF32X3); the default strict path
+// stays bit-exact.
+//
+// Each f32 operand is split into two TF32 values, x = hi + lo with
+// hi = rna(x) and lo = rna(x - hi), and C = A*B is accumulated in f32 as
+// Ahi*Bhi + Ahi*Blo + Alo*Bhi (the dropped Alo*Blo is ~2^-22 relative).
+//
+//  * split pass: A -> Ahi, Alo (row-major, K-major for the MMA) and
+//    B -> BhiT, BloT (transposed to N x K, K-major), into the context arena;
+//  * GEMM: one CTA per 128 x 256 tile of C, 192 threads in three roles:
+//      warp 0  TMA producer: four 2-D tiled loads per k-block (16 k, 64-byte
+//              swizzle) into a 4-stage shared-memory ring, one mbarrier per
+//              stage with the transaction byte count;
+//      warp 1  allocates 256 TMEM columns (the 128 x 256 f32 accumulator) and
+//              one lane issues tcgen05.mma kind::tf32 (M128 N256 K8): three
+//              products per k-step, two k-steps per stage; tcgen05.commit
+//              frees a stage when its MMAs have read it;
+//      warps 2-5 epilogue: wait for the final commit, tcgen05.ld the
+//              accumulator (each warp its 32-lane quarter), add the seed,
+//              store C.
+//  * no cluster multicast anywhere: every CTA fetches its own tiles.
+//
+// Every wait is bounded: a wait that runs out sets the device flag to
+// kDeviceTimeout (reported as MAPAL_ERR_TIMEOUT), all roles leave their
+// loops, in-flight copies and MMAs are waited for (bounded again) and TMEM
+// is freed before the CTA exits.
+#include <cuda.h>
+
 #include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr int kATile = BM * BK * 4;  // bytes of one A tile (hi or lo)
+constexpr int kBTile = BN * BK * 4;  // bytes of one B tile (hi or lo)
+constexpr int kStageBytes = 2 * kATile + 2 * kBTile;
+constexpr uint32_t kDeviceTimeout = 0x100u;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // a wait gives up after 2 s
+
+struct Smem {
+  // stage buffers first, each 1024-byte aligned (the swizzle pattern repeats
+  // every 512 bytes for the 64-byte swizzle)
+  uint8_t stage[STAGES][kStageBytes];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ uint32_t sa(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(sa(b)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(sa(b)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(sa(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait on a phase: false when kWaitLimitNs ran out, or (abort given)
+// when another role has aborted.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort) {
+  const uint64_t t0 = now_ns();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try(b, parity)) return true;
+    if ((i & 255) == 255) {
+      if (abort && *abort) return false;
+      if (now_ns() - t0 > kWaitLimitNs) return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          sa(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(sa(bar))
+      : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, 64-byte swizzle: rows of 64 bytes
+// (16 tf32), 8-row groups 512 bytes apart (SBO), LBO 16 bytes (unused for
+// swizzled K-major), version 1 (sm_100), layout type 4 = SWIZZLE_64B.
+__device__ __forceinline__ uint64_t smem_desc(const void* p) {
+  uint64_t addr = sa(p);
+  uint64_t d = 0;
+  d |= (addr & 0x3FFFFull) >> 4;          // start address
+  d |= (uint64_t)(16 >> 4) << 16;         // leading byte offset
+  d |= (uint64_t)(512 >> 4) << 32;        // stride byte offset
+  d |= 1ull << 46;                        // version
+  d |= 4ull << 61;                        // SWIZZLE_64B
+  return d;
+}
+
+// Instruction descriptor: D f32, A and B tf32, both K-major, N = 256, M = 128.
+constexpr uint32_t kIdesc = (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_tf32(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kIdesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(sa(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    mm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
+                     const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
+                     float* __restrict__ C, int M, int N, int K, long long ldc, float seed, unsigned* flag) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int KT = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(&sm.tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer ----
+    int issued = 0;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES && !mbar_wait(&sm.empty[s], ((kt / STAGES) - 1) & 1, abort)) {
+        *abort = 1;
+        break;
+      }
+      uint8_t* st = sm.stage[s];
+      mbar_expect_tx(&sm.full[s], kStageBytes);
+      const int k0 = kt * BK;
+      tma_load_2d(st, &map_ahi, k0, m0, &sm.full[s]);
+      tma_load_2d(st + kATile, &map_alo, k0, m0, &sm.full[s]);
+      tma_load_2d(st + 2 * kATile, &map_bhi, k0, n0, &sm.full[s]);
+      tma_load_2d(st + 2 * kATile + kBTile, &map_blo, k0, n0, &sm.full[s]);
+      ++issued;
+    }
+    if (*abort) {
+      // Let the copies already issued land before the CTA can exit.
+      for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt)
+        mbar_wait(&sm.full[kt % STAGES], (kt / STAGES) & 1, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    bool ok = true;
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (!mbar_wait(&sm.full[s], (kt / STAGES) & 1, abort)) {
+        *abort = 1;
+        ok = false;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint8_t* st = sm.stage[s];
+      const uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
+      const uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTile);
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint64_t adv = (uint64_t)((kk * 8 * 4) >> 4);  // 32 bytes along K
+        mma_tf32(tmem, ahi + adv, bhi + adv, (kt > 0 || kk > 0) ? 1u : 0u);
+        mma_tf32(tmem, ahi + adv, blo + adv, 1u);
+        mma_tf32(tmem, alo + adv, bhi + adv, 1u);
+      }
+      mma_commit(&sm.empty[s]);
+    }
+    // Final commit: arrives once every MMA issued above has completed.
+    mma_commit(&sm.acc_full);
+    (void)ok;
+  } else if (warp >= 2) {
+    // ---- epilogue: TMEM -> registers -> global ----
+    const int quarter = warp % 4;  // TMEM lanes 32*quarter .. +31 are this warp's
+    bool ready = mbar_wait(&sm.acc_full, 0, abort);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (!ready) {
+      *abort = 1;
+    } else {
+      const int row = m0 + quarter * 32 + lane;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+        if (row < M) {
+          float* crow = C + (long long)row * ldc + n0 + c0;
+          const int nvalid = N - (n0 + c0);
+          if (nvalid >= 32 && ((ldc & 3) == 0) && (((uintptr_t)C & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(crow + j) =
+                  make_float4(v[j] + seed, v[j + 1] + seed, v[j + 2] + seed, v[j + 3] + seed);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nvalid) crow[j] = v[j] + seed;
+          }
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (*abort) {
+    if (threadIdx.x == 0) atomicOr(flag, kDeviceTimeout);
+    // MMAs still in flight must finish before their TMEM is released.
+    if (warp == 1 && lane == 0) mbar_wait(&sm.acc_full, 0, nullptr);
+    __syncwarp();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// ---- split pass --------------------------------------------------------------------------
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// hi = rna(x), lo = rna(x - hi); non-finite values (and a hi that rounded up
+// past the f32 range) keep lo = 0 so they propagate as hi*B alone.
+__device__ __forceinline__ void split1(float x, float& hi, float& lo) {
+  hi = tf32_rna(x);
+  if (isinf(hi) && !isinf(x)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+  lo = isfinite(hi) ? tf32_rna(__fsub_rn(x, hi)) : 0.0f;
+}
+
+// A (M x K, row stride lda) -> hi, lo (M x K, row stride kp).
+__global__ void split_rows_kernel(const float* __restrict__ A, long long lda, int M, int K, float* __restrict__ hi,
+                                  float* __restrict__ lo, long long kp) {
+  const long long total = (long long)M * K;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const long long r = e / K, c = e % K;
+    float h, l;
+    split1(__ldg(A + r * lda + c), h, l);
+    hi[r * kp + c] = h;
+    lo[r * kp + c] = l;
+  }
+}
+
+// B (K x N, row stride ldb) -> hiT, loT (N x K, row stride kp): 32x32 tiles
+// through shared memory so both sides stay coalesced.
+__global__ void split_transpose_kernel(const float* __restrict__ B, long long ldb, int K, int N,
+                                       float* __restrict__ hiT, float* __restrict__ loT, long long kp) {
+  __shared__ float th[32][33], tl[32][33];
+  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+#pragma unroll
+  for (int p = 0; p < 32; p += 8) {
+    const int k = k0 + ty + p, n = n0 + tx;
+    float h = 0.f, l = 0.f;
+    if (k < K && n < N) split1(__ldg(B + (long long)k * ldb + n), h, l);
+    th[ty + p][tx] = h;
+    tl[ty + p][tx] = l;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int p = 0; p < 32; p += 8) {
+    const int n = n0 + ty + p, k = k0 + tx;
+    if (n < N && k < K) {
+      hiT[(long long)n * kp + k] = th[tx][ty + p];
+      loT[(long long)n * kp + k] = tl[tx][ty + p];
+    }
+  }
+}
+
+// ---- host: tensor maps ----------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  }
+  return fn;
+}
+
+// rows x K f32 matrix with row stride kp (elements), box = box_rows x BK.
+int make_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t K, uint64_t kp, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(MAPAL_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {kp * 4};
+  cuuint32_t box[2] = {BK, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(MAPAL_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return 0;
+}
+
+}  // namespace
 
 int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C, uint64_t M, uint64_t N,
                          uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed) {
-  (void)d; (void)A; (void)B; (void)C; (void)M; (void)N; (void)K; (void)lda; (void)ldb; (void)ldc;
-  (void)seed;
-  return set_error(MAPAL_ERR_UNSUPPORTED, "3xTF32 matmul not built yet");
+  if (M > 0x7fffffffull || N > 0x7fffffffull || K > 0x7fffffffull) return set_error(MAPAL_ERR_UNSUPPORTED, "too large");
+  if ((N + BN - 1) / BN > 0x7fffffffull || (M + BM - 1) / BM > 65535)
+    return set_error(MAPAL_ERR_UNSUPPORTED, "matmul grid too large");
+  const uint64_t kp = (K + 3) & ~3ull;  // TMA row strides must be multiples of 16 bytes
+  const uint64_t elems = (M + N) * kp;
+  MAPAL_TRY(arena_reserve(d, 2 * elems * sizeof(float) + 4096));
+  float* ahi = (float*)d.arena;
+  float* alo = ahi + M * kp;
+  float* bhi = alo + M * kp;
+  float* blo = bhi + N * kp;
+  // keep every operand base 16-byte aligned (kp is a multiple of 4 floats)
+  split_rows_kernel<<<stream_grid(M * K, 256, d.prof.sm_count, 8), 256, 0, d.stream>>>(A, (long long)lda, (int)M,
+                                                                                        (int)K, ahi, alo, (long long)kp);
+  dim3 tg((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
+  if (tg.y > 65535) return set_error(MAPAL_ERR_UNSUPPORTED, "K too large for the split pass");
+  split_transpose_kernel<<<tg, dim3(32, 8), 0, d.stream>>>(B, (long long)ldb, (int)K, (int)N, bhi, blo, (long long)kp);
+
+  CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+  MAPAL_TRY(make_map(&m_ahi, ahi, M, K, kp, BM));
+  MAPAL_TRY(make_map(&m_alo, alo, M, K, kp, BM));
+  MAPAL_TRY(make_map(&m_bhi, bhi, N, K, kp, BN));
+  MAPAL_TRY(make_map(&m_blo, blo, N, K, kp, BN));
+
+  const size_t smem = sizeof(Smem) + 1024;
+  static uint64_t attr_set = 0;
+  if (!(attr_set >> d.device & 1)) {
+    MAPAL_CUDA(cudaFuncSetAttribute(mm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set |= 1ull << d.device;
+  }
+  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+  mm_tf32x3_kernel<<<grid, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N, (int)K,
+                                                       (long long)ldc, seed, d.trap);
+  return 0;
 }

@@ -115,5 +115,5 @@ extern "C" int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSit
     local.a.len = m[i] ? (m[i] - 1) * site->a.ci + site->k : 0;
     MAPAL_TRY(tile_site_on(ctx, i, &local, A[i], B[i], C[i], mode));
   }
-  return finish_all(ctx, false);
+  return finish_all(ctx, mode == MAPAL_MATMUL_TF32X3);
 }

@@ -155,7 +155,7 @@ extern "C" int mapal_gpu_tile_site_f32(MapalGpuCtx* ctx, const MapalTileSite* si
   if (mode != MAPAL_MATMUL_STRICT && mode != MAPAL_MATMUL_TF32X3)
     return set_error(MAPAL_ERR_INVALID, "unknown matmul mode");
   MAPAL_TRY(tile_site_on(ctx, 0, site, a, b, out, mode));
-  return finish(ctx, 0, false);
+  return finish(ctx, 0, mode == MAPAL_MATMUL_TF32X3);
 }
 
 extern "C" int mapal_gpu_matmul_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* A,
@@ -167,7 +167,7 @@ extern "C" int mapal_gpu_matmul_f32(MapalGpuCtx* ctx, const MapalTileSite* site,
   if (site->k > 0 && !is_matmul(*site))
     return set_error(MAPAL_ERR_UNSUPPORTED, "record is not matmul-shaped (a{ci>=K, ck=1}, b{ck>=N, clane=1})");
   MAPAL_TRY(tile_site_on(ctx, 0, site, A, B, C, mode));
-  return finish(ctx, 0, false);
+  return finish(ctx, 0, mode == MAPAL_MATMUL_TF32X3);
 }
 
 extern "C" int mapal_gpu_fir_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* w,

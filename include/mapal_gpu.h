@@ -192,7 +192,9 @@ int mapal_gpu_ctx_world(MapalGpuCtx* ctx, int* nranks, int* rank);
 int mapal_gpu_profile(MapalGpuCtx* ctx, int local, MapalGpuProfile* out);
 
 /* Stream of local device `local` (a cudaStream_t). Replace it with a caller
- * stream to order this library's work with the caller's. */
+ * stream to order this library's work with the caller's; NULL selects the
+ * legacy default stream. The context's own stream is what get_stream returns
+ * before the first set_stream. */
 int mapal_gpu_get_stream(MapalGpuCtx* ctx, int local, void** stream);
 int mapal_gpu_set_stream(MapalGpuCtx* ctx, int local, void* stream);
 

@@ -1,10 +1,15 @@
-// f32x2.cuh — packed pairs of binary32 values for sm_100's two-lane FP32
-// instructions (PTX mul.rn.f32x2 / add.rn.f32x2). Each lane is one IEEE
-// round-to-nearest-even operation, exactly what __fmul_rn / __fadd_rn give
-// one value at a time; the explicit .rn keeps the compiler from contracting
-// a multiply and an add into an FMA. One instruction handles two lanes, so a
-// strict multiply-then-add costs one issue slot per value pair instead of
-// two per value, and leaves issue slots for the loads.
+// f32x2.cuh — packed pairs of binary32 values for sm_100's two-lane FP32 add
+// (PTX add.rn.f32x2), used by the strict (bit-exact) kernels.
+//
+// A strict MAC is acc = acc + (a * b) with both operations rounded to
+// nearest-even, never an FMA. On this toolchain the code generator fuses a
+// packed multiply (mul.rn.f32x2, or even fma.rn.f32x2 with a -0 addend)
+// followed by a packed add into a packed FMA, whatever -fmad says; a scalar
+// __fmul_rn feeding a packed add.rn.f32x2 stays two roundings (measured on
+// B200: bit-identical to the separately rounded CPU chain on 8192 random
+// 64-step chains, and the packed-packed forms matched the FMA chain instead).
+// So products are scalar __fmul_rn (documented never to merge into an FMA)
+// and only the accumulation is packed: 3 issue slots per 2 MACs instead of 4.
 #pragma once
 
 #include <stdint.h>
@@ -22,19 +27,15 @@ __device__ __forceinline__ f2 f2_splat(float v) { return f2_pack(v, v); }
 __device__ __forceinline__ float f2_lo(f2 v) {
   float lo, hi;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  (void)hi;
   return lo;
 }
 
 __device__ __forceinline__ float f2_hi(f2 v) {
   float lo, hi;
   asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  (void)lo;
   return hi;
-}
-
-__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
-  f2 r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
 }
 
 __device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
@@ -43,5 +44,8 @@ __device__ __forceinline__ f2 f2_add(f2 a, f2 b) {
   return r;
 }
 
-// acc + (a * b), two separately rounded operations per lane.
-__device__ __forceinline__ f2 f2_mac(f2 acc, f2 a, f2 b) { return f2_add(acc, f2_mul(a, b)); }
+// (acc.lo + a0*b0, acc.hi + a1*b1): two rounded scalar products, one packed
+// rounded add.
+__device__ __forceinline__ f2 f2_mac(f2 acc, float a0, float b0, float a1, float b1) {
+  return f2_add(acc, f2_pack(__fmul_rn(a0, b0), __fmul_rn(a1, b1)));
+}

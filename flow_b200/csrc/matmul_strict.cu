@@ -14,9 +14,10 @@
 //  * each thread owns TM x TN cells in registers and walks k in steps of 4:
 //    one 128-bit load brings 4 k-values of an A row, one brings 4 columns of
 //    a B row;
-//  * the multiply and the add of two neighbouring cells issue as one packed
-//    f32x2 instruction each (mul.rn / add.rn: two IEEE roundings, never an
-//    FMA), halving issue pressure so the FP32 pipe, not issue, is the bound;
+//  * the products are scalar rounded multiplies and the adds of two
+//    neighbouring cells issue as one packed f32x2 add (3 issue slots per 2
+//    MACs instead of 4), leaving issue slots for the loads so the FP32 pipe,
+//    not issue, is the bound;
 //  * no split-K: k is never partitioned, so no cell is reassociated.
 //
 // The roofline is the FP32 pipe at one operation per lane per clock
@@ -150,14 +151,12 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
           const float* brow = bs + (kq * 4 + kk) * G::kBStride;
           const float4 b0 = *reinterpret_cast<const float4*>(brow + tx * 4);
           const float4 b1 = *reinterpret_cast<const float4*>(brow + BN / 2 + tx * 4);
-          const f2 bq[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y),
-                            f2_pack(b1.z, b1.w)};
+          const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
           for (int i = 0; i < TM; ++i) {
             const float av = kk == 0 ? a[i].x : kk == 1 ? a[i].y : kk == 2 ? a[i].z : a[i].w;
-            const f2 a2 = f2_splat(av);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac(acc[i][q], a2, bq[q]);
+            for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac(acc[i][q], av, bv[2 * q], av, bv[2 * q + 1]);
           }
         }
       }
@@ -167,13 +166,12 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
         const float* brow = bs + kk * G::kBStride;
         const float4 b0 = *reinterpret_cast<const float4*>(brow + tx * 4);
         const float4 b1 = *reinterpret_cast<const float4*>(brow + BN / 2 + tx * 4);
-        const f2 bq[4] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y),
-                          f2_pack(b1.z, b1.w)};
+        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
         for (int i = 0; i < TM; ++i) {
-          const f2 a2 = f2_splat(as[a_row(i) * G::kAStride + kk]);
+          const float av = as[a_row(i) * G::kAStride + kk];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac(acc[i][q], a2, bq[q]);
+          for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac(acc[i][q], av, bv[2 * q], av, bv[2 * q + 1]);
         }
       }
     }

@@ -12,8 +12,8 @@
 //
 // Two outputs that are half a tile apart are computed as one packed pair
 // (f32x2): shared memory holds the input as pairs (x[j], x[j + half]), so
-// one 64-bit load feeds both lanes and one packed multiply and one packed
-// add advance two outputs by one tap.
+// one 64-bit load feeds both lanes; the two products are scalar rounded
+// multiplies and one packed rounded add advances both accumulators.
 #include "common.cuh"
 #include "f32x2.cuh"
 
@@ -32,12 +32,12 @@ __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restric
                                                           float* __restrict__ y, uint64_t n_out,
                                                           float seed) {
   extern __shared__ __align__(16) unsigned char fir_smem[];
-  f2* ws = reinterpret_cast<f2*>(fir_smem);  // (w[k], w[k])
-  const int span = kFirHalf + taps + kFirR;  // window pairs staged (tail padded)
-  f2* xs = ws + taps;                        // (x[t0 + j], x[t0 + half + j])
+  float* ws = reinterpret_cast<float*>(fir_smem);  // w[k]
+  const int span = kFirHalf + taps + kFirR;        // window pairs staged (tail padded)
+  f2* xs = reinterpret_cast<f2*>(ws + ((taps + 1) & ~1));  // (x[t0 + j], x[t0 + half + j])
   const uint64_t t0 = (uint64_t)blockIdx.x * kFirTile;
 
-  for (int k = threadIdx.x; k < taps; k += kFirThreads) ws[k] = f2_splat(w[k]);
+  for (int k = threadIdx.x; k < taps; k += kFirThreads) ws[k] = w[k];
   for (int j = threadIdx.x; j < span; j += kFirThreads) {
     uint64_t ia = t0 + j, ib = t0 + kFirHalf + j;
     float va = ia < x_len ? __ldg(x + ia) : 0.0f;
@@ -60,11 +60,11 @@ __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restric
 #pragma unroll
     for (int kk = 0; kk < kFirR; ++kk) {
       if (kg + kk < taps) {
-        const f2 w2 = ws[kg + kk];
+        const float wk = ws[kg + kk];
 #pragma unroll
         for (int r = 0; r < kFirR; ++r) {
           const f2 xv = (r + kk < kFirR) ? cur[r + kk] : nxt[r + kk - kFirR];
-          acc[r] = f2_mac(acc[r], w2, xv);
+          acc[r] = f2_mac(acc[r], wk, f2_lo(xv), wk, f2_hi(xv));
         }
       }
     }
@@ -104,9 +104,9 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
     bool rb = row < rows + 2 && cb < cols + 2 && ab < img_len;
     tile[r][c] = f2_pack(ra ? __ldg(img + aa) : 0.0f, rb ? __ldg(img + ab) : 0.0f);
   }
-  f2 w2[9];
+  float w9[9];
 #pragma unroll
-  for (int k = 0; k < 9; ++k) w2[k] = f2_splat(__ldg(w + k));
+  for (int k = 0; k < 9; ++k) w9[k] = __ldg(w + k);
   __syncthreads();
 
   const int c = threadIdx.x;
@@ -123,9 +123,9 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
     for (int dr = 0; dr < 3; ++dr) {
       const int p = r - dr;
       if (p >= 0 && p < kConvP) {
-        acc[p] = f2_mac(acc[p], w2[3 * dr + 0], v0);
-        acc[p] = f2_mac(acc[p], w2[3 * dr + 1], v1);
-        acc[p] = f2_mac(acc[p], w2[3 * dr + 2], v2);
+        acc[p] = f2_mac(acc[p], w9[3 * dr + 0], f2_lo(v0), w9[3 * dr + 0], f2_hi(v0));
+        acc[p] = f2_mac(acc[p], w9[3 * dr + 1], f2_lo(v1), w9[3 * dr + 1], f2_hi(v1));
+        acc[p] = f2_mac(acc[p], w9[3 * dr + 2], f2_lo(v2), w9[3 * dr + 2], f2_hi(v2));
       }
     }
   }
@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
 // Shared-memory bytes of one FIR block, 0 if the taps do not fit.
 static size_t fir_smem_bytes(uint64_t taps) {
   if (taps > 8192) return 0;
-  return sizeof(f2) * (size_t)(taps + kFirHalf + taps + kFirR);
+  return sizeof(float) * (size_t)((taps + 1) & ~1ull) + sizeof(f2) * (size_t)(kFirHalf + taps + kFirR);
 }
 
 int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, uint64_t x_len, float* y,

@@ -268,7 +268,7 @@ def run_ours(args) -> int:
     flush_out = torch.empty((), dtype=torch.float32, device="cuda")
 
     def flush():
-        torch.sum(flush_buf, dtype=torch.float32, out=flush_out)
+        torch.sum(flush_buf, dim=0, out=flush_out)
 
     mode = fb.TF32X3 if args.mode == "tf32x3" else fb.STRICT
     n = N_MM

@@ -264,6 +264,26 @@ int mapal_gpu_gather(MapalGpuCtx* ctx, const float* x, uint64_t n_x, const int32
  * within 1e-6 * sum|x| of the exact sum. */
 int mapal_gpu_fold_sum_f32(MapalGpuCtx* ctx, float seed, const float* x, uint64_t n, float* out);
 
+/* The same sum fold for callers that cannot allocate device memory: no
+ * context, and no cudaMalloc / cudaFree or other allocation anywhere in the
+ * call. This entry point has no counterpart in the reference.
+ * Who needs it: a host runtime that serves every device byte from one arena it
+ * sized up front and must not have a library allocate behind it, a process
+ * already at its HBM limit, or a latency-bound loop that cannot take
+ * cudaMalloc's implicit device synchronisation.
+ * Scratch: a fixed 8 KiB + 8 B array in the library's device data (1024 f64
+ * partial slots and a counter), present on every GPU that loads the library
+ * until the process exits. A device whose fold launch would need more than
+ * 1024 slots (more than 256 SMs) is refused with MAPAL_ERR_INVALID.
+ * Runs on the calling thread's current device, enqueued on `stream` (a
+ * cudaStream_t, NULL = default stream); returns after enqueueing, so read
+ * `out` (a device float) after synchronising the stream. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make
+ * that first call before any stream capture. Calls share the array: the
+ * counter is cleared on the stream before each launch, and calls whose
+ * kernels overlap on the GPU race and give wrong results. */
+int mapal_gpu_fold_sum_f32_noalloc(float seed, const float* x, uint64_t n, float* out, void* stream);
+
 /* FIR / window site (benches/shapes/fir_1048576.mapal:10-12):
  * site must be rows=1, a = taps {ck=1, ci=0, clane=0}, b = signal {ck=1, clane=1,
  * ci=0}: out[t] = fold_k(acc + w[k]*x[t+k]) from seed, k ascending. Bit-exact. */

@@ -467,8 +467,7 @@ def time_launches(torch, stream, fn, flush, reps: int) -> float:
 def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
     stream = torch.cuda.current_stream()
     hbm = pk["hbm_gbs"]
-    out = {"hbm_peak_gbs": hbm, "peak_source": pk["source"], "l2": "flushed before every launch"}
-    reps = 10
+    out = {"hbm_peak_gbs": hbm, "peak_source": pk["source"]}
 
     def rec(name, nbytes, ms, extra=None):
         gbs = nbytes / (ms * 1e-3) / 1e9
@@ -478,41 +477,27 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
         out[name] = r
 
     if d.world == 1:
-        n = 1 << 20
-        x = torch.empty(n, dtype=torch.float32, device="cuda")
-        y0 = torch.empty_like(x)
-        y = torch.empty_like(x)
-        ctx.gen(x, 1, 0)
-        ctx.gen(y0, 1, n)
-        rec("saxpy_2^20", 12 * n, time_launches(torch, stream, lambda: ctx.saxpy(2.5, x, y0, y), flush, reps))
-        side = 1024
-        tsite = fb.transpose_site(side, side)
-        rec("transpose_1024^2", 8 * side * side,
-            time_launches(torch, stream, lambda: ctx.transpose(tsite, x, y), flush, reps))
-        idx = torch.empty(n, dtype=torch.int32, device="cuda")
-        ctx.gen_index(idx, 1, n, n)
-        rec("gather_2^20", 12 * n, time_launches(torch, stream, lambda: ctx.gather(x, idx, y), flush, reps),
-            {"bytes_basis": "algorithmic 12 B/element"})
-        s = torch.empty(1, dtype=torch.float32, device="cuda")
-        xs = torch.empty(n, dtype=torch.float32, device="cuda")
-        ctx.gen(xs, 1, 0, fb.U01)
-        rec("sum_2^20", 4 * n, time_launches(torch, stream, lambda: ctx.fold_sum(xs, s), flush, reps))
-        taps = 64
-        n_out = n - taps + 1
-        w = torch.empty(taps, dtype=torch.float32, device="cuda")
-        ctx.gen(w, 1, n)
-        fsite = fb.fir_site(n_out, taps)
-        ms = time_launches(torch, stream, lambda: ctx.fir(fsite, w, x, y), flush, reps)
-        rec("fir_2^20x64", 4 * n + 4 * n_out + 4 * taps, ms,
-            {"flops": 2 * taps * n_out, "fp32_frac": 2 * taps * n_out / (ms * 1e-3) /
-             (ctx.profile().sm_count * 128 * pk["sm_max_mhz"] * 1e6)})
-        H = W = 1024
-        csite = fb.conv2d_site(H - 2, W - 2, W, H * W)
-        w9 = torch.empty(9, dtype=torch.float32, device="cuda")
-        ctx.gen(w9, 1, H * W)
-        rec("conv2d_1024^2_3x3", 4 * H * W + 4 * (H - 2) * (W - 2) + 36,
-            time_launches(torch, stream, lambda: ctx.conv2d_3x3(csite, w9, x, y), flush, reps))
-        del x, y0, y, idx, xs
+        # 2^20-class sites: back-to-back launches rotating
+        # over enough buffer sets to exceed twice the L2, so no launch finds
+        # its inputs in L2 (flow_b200.sitebench).
+        from flow_b200 import sitebench
+        l2 = ctx.profile().l2_bytes
+        sms = ctx.profile().sm_count
+        for key, site, size, k in [("saxpy_2^20", "saxpy", 1 << 20, None),
+                                   ("transpose_1024^2", "transpose", 1024 * 1024, None),
+                                   ("gather_2^20", "gather", 1 << 20, None),
+                                   ("sum_2^20", "sum", 1 << 20, None),
+                                   ("fir_2^20x64", "fir", 1 << 20, 64),
+                                   ("conv2d_1024^2_3x3", "conv2d", 1024 * 1024, None)]:
+            r = sitebench.measure(ctx, torch, site, size, k, reps=50, warmup=3, l2_bytes=l2)
+            extra = {"buffer_sets": r["buffer_sets"], "launches": r["launches"]}
+            if site == "gather":
+                extra["bytes_basis"] = "algorithmic 12 B/element"
+            if site == "fir":
+                extra["fp32_frac"] = r["gflops"] * 1e9 / (sms * 128 * pk["sm_max_mhz"] * 1e6)
+            rec(key, r["bytes"], r["ms"], extra)
+        out["l2"] = ("2^20 class: launches rotate over buffer sets totalling > 2x L2; "
+                     "2^30 class: inputs far larger than L2")
 
     # 2^30-class, sharded over the ranks (each rank its contiguous share).
     big = {}

@@ -44,6 +44,25 @@ BASELINE_TFLOPS = 2.40
 HBM_FALLBACK_GBS = 6650.0
 
 
+# stdout carries exactly one JSON line: everything else any library writes to
+# fd 1 (NCCL's version banner, for one) is sent to stderr, and the line goes
+# to the original stdout.
+_JSON_OUT = None
+
+
+def quiet_stdout() -> None:
+    global _JSON_OUT
+    sys.stdout.flush()
+    _JSON_OUT = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
+
+
+def emit_line(line: dict) -> None:
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def env_int(name: str, default: int) -> int:
     try:
         return int(os.environ.get(name, default))
@@ -197,7 +216,7 @@ def reference_arm(args) -> int:
         "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                                     "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit_line(line)
     return 0
 
 
@@ -445,7 +464,7 @@ def run_ours(args) -> int:
         "matmul_tf32x3": tf32, "streaming": streaming,
     }
     if d.rank == 0:
-        print(json.dumps(line), flush=True)
+        emit_line(line)
     ctx.close()
     d.close()
     return 0
@@ -549,6 +568,7 @@ def main() -> int:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--check", action="store_true", help="bit-exact spot check of one output row")
     args = ap.parse_args()
+    quiet_stdout()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
     if args.impl == "reference":

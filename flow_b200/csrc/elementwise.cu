@@ -84,25 +84,44 @@ __global__ void zip_scalar_kernel(int op, const float* __restrict__ x, const flo
 // widened with sign and compared two-sided; a miss stores kind+1 = 2 into
 // the trap flag and skips the element. idx/out move as int4/float4; the x
 // reads are data-dependent 4-byte loads through the read-only path.
+__device__ __forceinline__ bool in_range(int4 j, int64_t n_x) {
+  return (int64_t)j.x >= 0 && (int64_t)j.x < n_x && (int64_t)j.y >= 0 && (int64_t)j.y < n_x &&
+         (int64_t)j.z >= 0 && (int64_t)j.z < n_x && (int64_t)j.w >= 0 && (int64_t)j.w < n_x;
+}
+
+// Random x reads: read-only path, no L1 allocation (a gathered line is
+// rarely reused by the same SM).
+__device__ __forceinline__ float ld_gather(const float* p) {
+  float v;
+  asm volatile("ld.global.nc.L1::no_allocate.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ float4 gather4(const float* __restrict__ x, int4 j) {
+  return make_float4(ld_gather(x + j.x), ld_gather(x + j.y), ld_gather(x + j.z), ld_gather(x + j.w));
+}
+
+// Two index groups per trip, so eight independent x reads are in flight per
+// thread behind the two index loads.
 __global__ void __launch_bounds__(kThreads) gather_vec_kernel(const float* __restrict__ x, int64_t n_x,
                                                               const int4* __restrict__ idx,
                                                               float4* __restrict__ out, uint64_t n4,
                                                               unsigned* trap) {
-  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n4;
-       i += (uint64_t)gridDim.x * blockDim.x) {
-    int4 j = __ldcs(idx + i);
-    bool ok = (int64_t)j.x >= 0 && (int64_t)j.x < n_x && (int64_t)j.y >= 0 && (int64_t)j.y < n_x &&
-              (int64_t)j.z >= 0 && (int64_t)j.z < n_x && (int64_t)j.w >= 0 && (int64_t)j.w < n_x;
-    if (!ok) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
+  for (; i + stride < n4; i += 2 * stride) {
+    const int4 ja = __ldcs(idx + i), jb = __ldcs(idx + i + stride);
+    const bool oka = in_range(ja, n_x), okb = in_range(jb, n_x);
+    if (!oka || !okb) *trap = 2u;
+    if (oka) st_stream(out + i, gather4(x, ja));
+    if (okb) st_stream(out + i + stride, gather4(x, jb));
+  }
+  if (i < n4) {
+    const int4 ja = __ldcs(idx + i);
+    if (in_range(ja, n_x))
+      st_stream(out + i, gather4(x, ja));
+    else
       *trap = 2u;
-      continue;
-    }
-    float4 r;
-    r.x = __ldg(x + j.x);
-    r.y = __ldg(x + j.y);
-    r.z = __ldg(x + j.z);
-    r.w = __ldg(x + j.w);
-    st_stream(out + i, r);
   }
 }
 
@@ -180,7 +199,7 @@ int launch_gather(cudaStream_t s, int sms, const float* x, uint64_t n_x, const i
   if (aligned16(idx) && aligned16(out)) {
     uint64_t n4 = n / 4;
     if (n4) {
-      gather_vec_kernel<<<stream_grid(n4, kThreads, sms, 8), kThreads, 0, s>>>(
+      gather_vec_kernel<<<stream_grid((n4 + 1) / 2, kThreads, sms, 8), kThreads, 0, s>>>(
           x, (int64_t)n_x, (const int4*)idx, (float4*)out, n4, trap);
       done = n4 * 4;
     }

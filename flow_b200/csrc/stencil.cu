@@ -5,16 +5,16 @@
 // crates/backends/llvm/tests/snapshots/tile_sites_pin__tile_record_content.snap).
 // The reference evaluates each output as a per-thread loop over global memory
 // (crates/backends/cuda/src/kernel.rs:2773-2886). Here a block stages its
-// input window once in shared memory and each thread keeps a sliding window
-// of inputs in registers. Every output keeps its exact fold order (acc from
-// the seed, then acc + w[k]*x[...] for k ascending, each op rounded), so the
+// input window once into shared memory with asynchronous copies (all of a
+// block's loads in flight at once) and each thread keeps a sliding window of
+// inputs in registers. Every output keeps its exact fold order (acc from the
+// seed, then acc + w[k]*x[...] for k ascending, each op rounded), so the
 // results are bit-identical to the interpreter's.
 //
-// Two outputs that are half a tile apart are computed as one packed pair
-// (f32x2): shared memory holds the input as pairs (x[j], x[j + half]), so
-// one 64-bit load feeds both lanes; the two products are scalar rounded
-// multiplies and one packed rounded add advances both accumulators.
+// Each thread computes two outputs half a tile apart as one packed pair: two
+// scalar rounded products and one packed rounded add (f32x2.cuh).
 #include "common.cuh"
+#include "cpasync.cuh"
 #include "f32x2.cuh"
 
 namespace {
@@ -22,58 +22,76 @@ namespace {
 // ---- FIR ---------------------------------------------------------------------
 
 constexpr int kFirThreads = 64;
-constexpr int kFirR = 8;                              // outputs per thread per lane
-constexpr int kFirHalf = kFirThreads * kFirR;         // outputs per lane per block
-constexpr int kFirTile = 2 * kFirHalf;                // outputs per block
+constexpr int kFirR = 8;                       // outputs per thread per lane
+constexpr int kFirHalf = kFirThreads * kFirR;  // outputs per lane per block
+constexpr int kFirTile = 2 * kFirHalf;         // outputs per block
+
+__host__ __device__ constexpr int fir_wpad(int taps) { return (taps + 7) & ~7; }
 
 // y[t] = fold_k(acc + w[k] * x[t + k]) from seed, t in [0, n_out).
 __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restrict__ w, int taps,
                                                           const float* __restrict__ x, uint64_t x_len,
                                                           float* __restrict__ y, uint64_t n_out,
                                                           float seed) {
-  extern __shared__ __align__(16) unsigned char fir_smem[];
-  float* ws = reinterpret_cast<float*>(fir_smem);  // w[k]
-  const int span = kFirHalf + taps + kFirR;        // window pairs staged (tail padded)
-  f2* xs = reinterpret_cast<f2*>(ws + ((taps + 1) & ~1));  // (x[t0 + j], x[t0 + half + j])
+  extern __shared__ __align__(16) float fir_smem[];
+  float* ws = fir_smem;                    // taps, zero-padded to a multiple of 8
+  float* xs = fir_smem + fir_wpad(taps);   // x[t0 .. t0 + tile + taps + 16)
+  const int span = (kFirTile + taps + 16 + 3) & ~3;  // staged floats, whole 16-byte groups
   const uint64_t t0 = (uint64_t)blockIdx.x * kFirTile;
+  const bool xal = ((uintptr_t)x & 15) == 0, wal = ((uintptr_t)w & 15) == 0;
 
-  for (int k = threadIdx.x; k < taps; k += kFirThreads) ws[k] = w[k];
-  for (int j = threadIdx.x; j < span; j += kFirThreads) {
-    uint64_t ia = t0 + j, ib = t0 + kFirHalf + j;
-    float va = ia < x_len ? __ldg(x + ia) : 0.0f;
-    float vb = ib < x_len ? __ldg(x + ib) : 0.0f;
-    xs[j] = f2_pack(va, vb);
+  for (int c = threadIdx.x; c < fir_wpad(taps) / 4; c += kFirThreads) {
+    const int k = 4 * c;
+    copy4(smem_u32(ws + k), w + (k < taps ? k : 0), taps - k, wal);
   }
+  for (int c = threadIdx.x; c < span / 4; c += kFirThreads) {
+    const uint64_t g = t0 + 4 * (uint64_t)c;
+    const int nvalid = g < x_len ? (int)(x_len - g < 4 ? x_len - g : 4) : 0;
+    copy4(smem_u32(xs + 4 * c), x + (nvalid > 0 ? g : 0), nvalid, xal);
+  }
+  cp_commit();
+  cp_wait<0>();
   __syncthreads();
 
-  const int base = threadIdx.x * kFirR;
+  const int ba = threadIdx.x * kFirR, bb = kFirHalf + threadIdx.x * kFirR;
   f2 acc[kFirR];
   const f2 s2 = f2_splat(seed);
 #pragma unroll
   for (int r = 0; r < kFirR; ++r) acc[r] = s2;
-  f2 cur[kFirR], nxt[kFirR];
+  float ca[kFirR], cb[kFirR], na[kFirR], nb[kFirR];
 #pragma unroll
-  for (int r = 0; r < kFirR; ++r) cur[r] = xs[base + r];
+  for (int r = 0; r < kFirR; r += 4) {
+    *reinterpret_cast<float4*>(ca + r) = *reinterpret_cast<const float4*>(xs + ba + r);
+    *reinterpret_cast<float4*>(cb + r) = *reinterpret_cast<const float4*>(xs + bb + r);
+  }
   for (int kg = 0; kg < taps; kg += kFirR) {
+    float w8[kFirR];
 #pragma unroll
-    for (int r = 0; r < kFirR; ++r) nxt[r] = xs[base + kg + kFirR + r];
+    for (int r = 0; r < kFirR; r += 4) {
+      *reinterpret_cast<float4*>(na + r) = *reinterpret_cast<const float4*>(xs + ba + kg + kFirR + r);
+      *reinterpret_cast<float4*>(nb + r) = *reinterpret_cast<const float4*>(xs + bb + kg + kFirR + r);
+      *reinterpret_cast<float4*>(w8 + r) = *reinterpret_cast<const float4*>(ws + kg + r);
+    }
 #pragma unroll
     for (int kk = 0; kk < kFirR; ++kk) {
       if (kg + kk < taps) {
-        const float wk = ws[kg + kk];
 #pragma unroll
         for (int r = 0; r < kFirR; ++r) {
-          const f2 xv = (r + kk < kFirR) ? cur[r + kk] : nxt[r + kk - kFirR];
-          acc[r] = f2_mac(acc[r], wk, f2_lo(xv), wk, f2_hi(xv));
+          const float xa = (r + kk < kFirR) ? ca[r + kk] : na[r + kk - kFirR];
+          const float xb = (r + kk < kFirR) ? cb[r + kk] : nb[r + kk - kFirR];
+          acc[r] = f2_mac(acc[r], w8[kk], xa, w8[kk], xb);
         }
       }
     }
 #pragma unroll
-    for (int r = 0; r < kFirR; ++r) cur[r] = nxt[r];
+    for (int r = 0; r < kFirR; ++r) {
+      ca[r] = na[r];
+      cb[r] = nb[r];
+    }
   }
 #pragma unroll
   for (int r = 0; r < kFirR; ++r) {
-    uint64_t ta = t0 + base + r, tb = t0 + kFirHalf + base + r;
+    const uint64_t ta = t0 + ba + r, tb = t0 + bb + r;
     if (ta < n_out) y[ta] = f2_lo(acc[r]);
     if (tb < n_out) y[tb] = f2_hi(acc[r]);
   }
@@ -81,10 +99,11 @@ __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restric
 
 // ---- conv2d 3x3 ---------------------------------------------------------------
 
-constexpr int kConvThreads = 64;   // one thread per column pair
+constexpr int kConvThreads = 64;         // one thread per column pair
 constexpr int kConvHalf = kConvThreads;  // column pairs per block -> 128 columns
-constexpr int kConvP = 8;          // output rows per thread
+constexpr int kConvP = 8;                // output rows per thread
 constexpr int kConvCols = 2 * kConvHalf;
+constexpr int kConvPitch = kConvCols + 4;  // 130 used, 16-byte rows
 
 // out[i, j] = fold_k(acc + w[k] * img[(i + k/3)*stride + j + k%3]) from seed.
 __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __restrict__ w,
@@ -92,21 +111,29 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
                                                                uint64_t img_len, uint64_t stride,
                                                                float* __restrict__ out, uint64_t rows,
                                                                uint64_t cols, float seed) {
-  __shared__ f2 tile[kConvP + 2][kConvHalf + 2];
+  __shared__ __align__(16) float tile[kConvP + 2][kConvPitch];
   const uint64_t i0 = (uint64_t)blockIdx.y * kConvP;
   const uint64_t j0 = (uint64_t)blockIdx.x * kConvCols;
-  for (int e = threadIdx.x; e < (kConvP + 2) * (kConvHalf + 2); e += kConvThreads) {
-    int r = e / (kConvHalf + 2), c = e % (kConvHalf + 2);
-    uint64_t row = i0 + r;
-    uint64_t ca = j0 + c, cb = j0 + kConvHalf + c;
-    uint64_t aa = row * stride + ca, ab = row * stride + cb;
-    bool ra = row < rows + 2 && ca < cols + 2 && aa < img_len;
-    bool rb = row < rows + 2 && cb < cols + 2 && ab < img_len;
-    tile[r][c] = f2_pack(ra ? __ldg(img + aa) : 0.0f, rb ? __ldg(img + ab) : 0.0f);
+  const bool al = ((uintptr_t)img & 15) == 0 && (stride & 3) == 0;
+  constexpr int kChunks = kConvPitch / 4;
+  for (int e = threadIdx.x; e < (kConvP + 2) * kChunks; e += kConvThreads) {
+    const int r = e / kChunks, c = 4 * (e % kChunks);
+    const uint64_t row = i0 + r, col = j0 + c;
+    int nvalid = 0;
+    uint64_t g = 0;
+    if (row < rows + 2 && col < cols + 2) {
+      g = row * stride + col;
+      const uint64_t lim_row = cols + 2 - col, lim_len = g < img_len ? img_len - g : 0;
+      const uint64_t lim = lim_row < lim_len ? lim_row : lim_len;
+      nvalid = (int)(lim < 4 ? lim : 4);
+    }
+    copy4(smem_u32(&tile[r][c]), img + (nvalid > 0 ? g : 0), nvalid, al);
   }
+  cp_commit();
   float w9[9];
 #pragma unroll
   for (int k = 0; k < 9; ++k) w9[k] = __ldg(w + k);
+  cp_wait<0>();
   __syncthreads();
 
   const int c = threadIdx.x;
@@ -118,20 +145,21 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
   // applies each output's taps in ascending k (k = 3*dr + dc, dr = r - p).
 #pragma unroll
   for (int r = 0; r < kConvP + 2; ++r) {
-    const f2 v0 = tile[r][c], v1 = tile[r][c + 1], v2 = tile[r][c + 2];
+    const float a0 = tile[r][c], a1 = tile[r][c + 1], a2 = tile[r][c + 2];
+    const float b0 = tile[r][kConvHalf + c], b1 = tile[r][kConvHalf + c + 1], b2 = tile[r][kConvHalf + c + 2];
 #pragma unroll
     for (int dr = 0; dr < 3; ++dr) {
       const int p = r - dr;
       if (p >= 0 && p < kConvP) {
-        acc[p] = f2_mac(acc[p], w9[3 * dr + 0], f2_lo(v0), w9[3 * dr + 0], f2_hi(v0));
-        acc[p] = f2_mac(acc[p], w9[3 * dr + 1], f2_lo(v1), w9[3 * dr + 1], f2_hi(v1));
-        acc[p] = f2_mac(acc[p], w9[3 * dr + 2], f2_lo(v2), w9[3 * dr + 2], f2_hi(v2));
+        acc[p] = f2_mac(acc[p], w9[3 * dr + 0], a0, w9[3 * dr + 0], b0);
+        acc[p] = f2_mac(acc[p], w9[3 * dr + 1], a1, w9[3 * dr + 1], b1);
+        acc[p] = f2_mac(acc[p], w9[3 * dr + 2], a2, w9[3 * dr + 2], b2);
       }
     }
   }
 #pragma unroll
   for (int p = 0; p < kConvP; ++p) {
-    uint64_t i = i0 + p, ja = j0 + c, jb = j0 + kConvHalf + c;
+    const uint64_t i = i0 + p, ja = j0 + c, jb = j0 + kConvHalf + c;
     if (i < rows) {
       if (ja < cols) out[i * cols + ja] = f2_lo(acc[p]);
       if (jb < cols) out[i * cols + jb] = f2_hi(acc[p]);
@@ -144,7 +172,7 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
 // Shared-memory bytes of one FIR block, 0 if the taps do not fit.
 static size_t fir_smem_bytes(uint64_t taps) {
   if (taps > 8192) return 0;
-  return sizeof(float) * (size_t)((taps + 1) & ~1ull) + sizeof(f2) * (size_t)(kFirHalf + taps + kFirR);
+  return sizeof(float) * ((size_t)fir_wpad((int)taps) + (((size_t)kFirTile + (size_t)taps + 16 + 3) & ~(size_t)3));
 }
 
 int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, uint64_t x_len, float* y,

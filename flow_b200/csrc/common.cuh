@@ -52,6 +52,10 @@ struct DeviceSlot {
   void* arena = nullptr;
   size_t arena_bytes = 0;
   ncclComm_t comm = nullptr;
+  // Collectives that overlap compute run on this stream, ordered against
+  // `stream` with events from `events` (created on first use, reused).
+  cudaStream_t comm_stream = nullptr;
+  std::vector<cudaEvent_t> events;
   MapalGpuProfile prof{};
 };
 
@@ -114,5 +118,15 @@ int launch_fold_sum(cudaStream_t s, int sms, const float* x, uint64_t n, float s
 int launch_finalize_sum(cudaStream_t s, const double* total, float seed, float* out);
 int launch_matmul_strict(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
                          uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed);
+int launch_matmul_strict_ex(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
+                            uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed,
+                            int acc_from_c);
+// Record checks of tile.cu: status, and whether the record is matmul-shaped.
+int validate_tile_site(const MapalTileSite* site, const void* a, const void* b, const void* out, bool* empty,
+                       bool* matmul_shaped);
+// At least n reusable events on a device slot; the comm stream on first use.
+int slot_events(DeviceSlot& d, size_t n);
+int nccl_broadcast_f32_on(MapalGpuCtx* ctx, float* const* buf, size_t offset, size_t count, int root,
+                          bool on_comm);
 int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C, uint64_t M,
                          uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed);

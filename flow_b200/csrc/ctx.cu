@@ -160,8 +160,24 @@ static void free_slot(DeviceSlot& d) {
   cudaFree(d.fold_counter);
   cudaFree(d.fold_total);
   cudaFree(d.arena);
+  if (d.comm_stream) {
+    cudaStreamSynchronize(d.comm_stream);
+    cudaStreamDestroy(d.comm_stream);
+  }
+  for (cudaEvent_t e : d.events) cudaEventDestroy(e);
   if (d.own_stream) cudaStreamDestroy(d.own_stream);
   d = DeviceSlot{};
+}
+
+int slot_events(DeviceSlot& d, size_t n) {
+  MAPAL_CUDA(cudaSetDevice(d.device));
+  if (!d.comm_stream) MAPAL_CUDA(cudaStreamCreateWithFlags(&d.comm_stream, cudaStreamNonBlocking));
+  while (d.events.size() < n) {
+    cudaEvent_t e;
+    MAPAL_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    d.events.push_back(e);
+  }
+  return 0;
 }
 
 extern "C" int mapal_gpu_ctx_create(uint32_t device_mask, MapalGpuCtx** out) {
@@ -394,6 +410,13 @@ int nccl_allreduce_f64(MapalGpuCtx* ctx, double* const* buf, size_t count) {
 }
 
 int nccl_broadcast_f32(MapalGpuCtx* ctx, float* const* buf, size_t count, int root) {
+  return nccl_broadcast_f32_on(ctx, buf, 0, count, root, false);
+}
+
+// Broadcast buf[i][offset, offset + count) from `root` on every local device,
+// on the devices' comm streams when on_comm (slot_events must have run).
+int nccl_broadcast_f32_on(MapalGpuCtx* ctx, float* const* buf, size_t offset, size_t count, int root,
+                          bool on_comm) {
   NcclApi* n = nccl_api();
   if (ctx->nranks == 1) return 0;
   if (!n->loaded) return set_error(MAPAL_ERR_NCCL, n->error);
@@ -401,7 +424,8 @@ int nccl_broadcast_f32(MapalGpuCtx* ctx, float* const* buf, size_t count, int ro
   if (rc) return nccl_fail(rc, "ncclGroupStart");
   for (auto i = 0u; i < ctx->dev.size(); ++i) {
     DeviceSlot& d = ctx->dev[i];
-    rc = n->Broadcast(buf[i], buf[i], count, kNcclFloat32, root, d.comm, d.stream);
+    rc = n->Broadcast(buf[i] + offset, buf[i] + offset, count, kNcclFloat32, root, d.comm,
+                      on_comm ? d.comm_stream : d.stream);
     if (rc) {
       n->GroupEnd();
       return nccl_fail(rc, "ncclBroadcast");

@@ -74,10 +74,17 @@ struct Cfg {
   static_assert(BK % 4 == 0, "k advances in steps of 4");
 };
 
+// Work is laid out on a grid of 128 x 128 parent tiles (tiles_n0 per row of
+// tiles). A CTA of this instance covers one (128/BM)^2-th of a parent tile:
+// CTA u takes sub-tile u % split^2 of parent tile tile_base + u / split^2.
+// With acc_from_c the cells start from the values already in C (a partial
+// fold carried over from an earlier k range, bit-exact because the carried
+// accumulator is the same f32 value) instead of from the seed.
 template <int BM, int BN, int BK, int TM, int TN, int STAGES, bool kVec>
 __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
     mm_strict_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
-                     int M, int N, int K, long long lda, long long ldb, long long ldc, float seed) {
+                     int M, int N, int K, long long lda, long long ldb, long long ldc, float seed,
+                     int tile_base, int tiles_n0, int acc_from_c) {
   using G = Cfg<BM, BN, BK, TM, TN, STAGES>;
   extern __shared__ __align__(16) float smem[];
   float* As = smem;                              // [STAGES][BM][kAStride]
@@ -85,7 +92,12 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
 
   const int tid = threadIdx.x;
   const int tx = tid % G::kThreadsN, ty = tid / G::kThreadsN;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  constexpr int kSplit = 128 / BM;
+  static_assert(BM == BN && 128 % BM == 0, "square CTA tiles that divide the 128 x 128 parent tile");
+  const int parent = tile_base + (int)blockIdx.x / (kSplit * kSplit);
+  const int sub = (int)blockIdx.x % (kSplit * kSplit);
+  const int m0 = (parent / tiles_n0) * 128 + (sub / kSplit) * BM;
+  const int n0 = (parent % tiles_n0) * 128 + (sub % kSplit) * BN;
   const int KT = (K + BK - 1) / BK;
 
   // Loader coordinates: A tile BM x BK in 16-byte groups, B tile BK x BN.
@@ -121,6 +133,21 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
 
   // Row i of the thread tile: quadrant rows ty*4 + i (i < 4) and BM/2 + ty*4 + i-4.
   auto a_row = [&](int i) { return (i < 4 ? 0 : BM / 2) + ty * 4 + (i & 3); };
+
+  if (acc_from_c) {
+#pragma unroll
+    for (int i = 0; i < TM; ++i) {
+      const int m = m0 + a_row(i);
+#pragma unroll
+      for (int q = 0; q < TN / 2; ++q) {
+        const int n = n0 + (q < 2 ? 0 : BN / 2) + tx * 4 + 2 * (q & 1);
+        const float* cp = C + (long long)(m < M ? m : 0) * ldc;
+        const float lo = (m < M && n < N) ? cp[n] : 0.0f;
+        const float hi = (m < M && n + 1 < N) ? cp[n + 1] : 0.0f;
+        acc[i][q] = f2_pack(lo, hi);
+      }
+    }
+  }
 
 #pragma unroll
   for (int s = 0; s < STAGES - 1; ++s) {
@@ -200,9 +227,11 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
   }
 }
 
+// Launch `ntiles` parent tiles starting at tile_base, each as (128/BM)^2 CTAs.
 template <int BM, int BN, int BK, int STAGES, bool kVec>
 int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_t M, uint64_t N,
-               uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed) {
+               uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed, int tile_base, int ntiles,
+               int tiles_n0, int acc_from_c) {
   using G = Cfg<BM, BN, BK, 8, 8, STAGES>;
   auto kern = mm_strict_kernel<BM, BN, BK, 8, 8, STAGES, kVec>;
   static uint64_t attr_set = 0;  // per template instance, one bit per device
@@ -213,26 +242,46 @@ int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(mm_strict)");
     attr_set |= 1ull << dev;
   }
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  kern<<<grid, G::kThreads, G::kSmem, s>>>(A, B, C, (int)M, (int)N, (int)K, (long long)lda,
-                                           (long long)ldb, (long long)ldc, seed);
+  constexpr int kSplit = 128 / BM;
+  const unsigned grid = (unsigned)ntiles * kSplit * kSplit;
+  if (grid == 0) return 0;
+  kern<<<grid, G::kThreads, G::kSmem, s>>>(A, B, C, (int)M, (int)N, (int)K, (long long)lda, (long long)ldb,
+                                           (long long)ldc, seed, tile_base, tiles_n0, acc_from_c);
   return 0;
+}
+
+template <bool kVec>
+int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M, uint64_t N,
+                    uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed, int acc_from_c) {
+  const int tiles_n0 = (int)((N + 127) / 128);
+  const int tiles = (int)((M + 127) / 128) * tiles_n0;
+  // Whole waves of 128 x 128 CTAs (one per SM); the leftover tiles, which
+  // would run as a partly empty last wave, go as four 64 x 64 CTAs each so
+  // the last wave's work spreads over every SM.
+  const int full = (tiles / sms) * sms;
+  MAPAL_TRY((launch_cfg<128, 128, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
+                                                acc_from_c)));
+  return launch_cfg<64, 64, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, full, tiles - full,
+                                         tiles_n0, acc_from_c);
 }
 
 }  // namespace
 
-// Tile choice: the largest CTA tile that still gives every SM work for
-// about two waves; smaller problems take 64-row tiles so more SMs are busy.
-int launch_matmul_strict(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
-                         uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed) {
+// The whole site as whole waves of 128 x 128 tiles plus a remainder in
+// 64 x 64 tiles. With acc_from_c, cells continue from the partial folds
+// stored in C (used to split K into ranges that overlap a B broadcast).
+int launch_matmul_strict_ex(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
+                            uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed,
+                            int acc_from_c) {
   if (M > 0x7fffffffull || N > 0x7fffffffull || K > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
+  if ((M + 127) / 128 * ((N + 127) / 128) > 0x7fffffffull / 4) return MAPAL_ERR_UNSUPPORTED;
   const bool vec = aligned16(A) && aligned16(B) && aligned16(C) && lda % 4 == 0 && ldb % 4 == 0 &&
                    ldc % 4 == 0;
-  const uint64_t tiles128 = ((M + 127) / 128) * ((N + 127) / 128);
-  if (tiles128 >= (uint64_t)sms * 2) {
-    return vec ? launch_cfg<128, 128, 16, 4, true>(s, A, B, C, M, N, K, lda, ldb, ldc, seed)
-               : launch_cfg<128, 128, 16, 4, false>(s, A, B, C, M, N, K, lda, ldb, ldc, seed);
-  }
-  return vec ? launch_cfg<64, 64, 16, 4, true>(s, A, B, C, M, N, K, lda, ldb, ldc, seed)
-             : launch_cfg<64, 64, 16, 4, false>(s, A, B, C, M, N, K, lda, ldb, ldc, seed);
+  return vec ? launch_balanced<true>(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, acc_from_c)
+             : launch_balanced<false>(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, acc_from_c);
+}
+
+int launch_matmul_strict(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
+                         uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed) {
+  return launch_matmul_strict_ex(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, 0);
 }

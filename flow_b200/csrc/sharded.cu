@@ -36,6 +36,64 @@ int check_arrays(MapalGpuCtx* ctx, const void* a, const void* b, const void* c) 
   return 0;
 }
 
+// Strict row-block matmul with the B broadcast overlapped: K is cut into
+// kChunks ranges; the broadcast of B's rows for range c runs on the comm
+// stream while range c-1 is multiplied on the compute stream. Range c > 0
+// continues every cell from the partial fold range c-1 left in C, so each
+// cell still folds k = 0..K-1 in order from the seed: bit-identical to one
+// pass.
+constexpr int kChunks = 4;
+
+int matmul_sharded_overlapped(MapalGpuCtx* ctx, const MapalTileSite* site, const float* const* A,
+                              float* const* B, float* const* C, const uint64_t* m, int root) {
+  const uint64_t K = site->k, lda = site->a.ci, ldb = site->b.ck, N = site->c;
+  const int nd = (int)ctx->dev.size();
+  // Validate every device's record before anything is enqueued.
+  for (int i = 0; i < nd; ++i) {
+    MapalTileSite local = *site;
+    local.rows = m[i];
+    local.a.base = 0;
+    local.a.len = m[i] ? (m[i] - 1) * lda + K : 0;
+    bool empty = false, mm = false;
+    MAPAL_TRY(validate_tile_site(&local, A[i], B[i], C[i], &empty, &mm));
+    if (!empty && !mm) return set_error(MAPAL_ERR_UNSUPPORTED, "record is not matmul-shaped");
+  }
+  // The broadcast must not overwrite B while earlier work on the compute
+  // stream may still read it.
+  for (int i = 0; i < nd; ++i) {
+    DeviceSlot& d = ctx->dev[i];
+    MAPAL_TRY(enter(ctx, i));
+    MAPAL_TRY(slot_events(d, kChunks + 1));
+    MAPAL_CUDA(cudaEventRecord(d.events[kChunks], d.stream));
+    MAPAL_CUDA(cudaStreamWaitEvent(d.comm_stream, d.events[kChunks], 0));
+  }
+  uint64_t k_lo[kChunks + 1];
+  for (int c = 0; c <= kChunks; ++c) k_lo[c] = K * (uint64_t)c / kChunks;
+  for (int c = 0; c < kChunks; ++c) {
+    // B rows [k_lo[c], k_lo[c+1]) within the B record's extent.
+    const uint64_t lo = site->b.base + k_lo[c] * ldb;
+    uint64_t hi = site->b.base + k_lo[c + 1] * ldb;
+    if (c == kChunks - 1 || hi > site->b.len) hi = site->b.len;
+    MAPAL_TRY(nccl_broadcast_f32_on(ctx, B, lo, hi - lo, root, true));
+    for (int i = 0; i < nd; ++i) {
+      MAPAL_TRY(enter(ctx, i));
+      MAPAL_CUDA(cudaEventRecord(ctx->dev[i].events[c], ctx->dev[i].comm_stream));
+    }
+  }
+  for (int c = 0; c < kChunks; ++c) {
+    for (int i = 0; i < nd; ++i) {
+      DeviceSlot& d = ctx->dev[i];
+      MAPAL_TRY(enter(ctx, i));
+      MAPAL_CUDA(cudaStreamWaitEvent(d.stream, d.events[c], 0));
+      if (m[i] == 0) continue;
+      const uint64_t k0 = k_lo[c], kc = k_lo[c + 1] - k_lo[c];
+      MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, A[i] + k0, B[i] + site->b.base + k0 * ldb,
+                                        C[i], m[i], N, kc, lda, ldb, N, site->seed, c > 0 ? 1 : 0));
+    }
+  }
+  return finish_all(ctx, false);
+}
+
 }  // namespace
 
 extern "C" int mapal_gpu_saxpy_sharded(MapalGpuCtx* ctx, float a, const float* const* x,
@@ -102,8 +160,10 @@ extern "C" int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSit
   if (mode != MAPAL_MATMUL_STRICT && mode != MAPAL_MATMUL_TF32X3)
     return set_error(MAPAL_ERR_INVALID, "unknown matmul mode");
   if (root < 0 || root >= ctx->nranks) return set_error(MAPAL_ERR_INVALID, "root out of range");
-  // B is replicated first: every rank's full B buffer receives root's.
   const uint64_t b_elems = site->b.len;
+  if (mode == MAPAL_MATMUL_STRICT && ctx->nranks > 1 && site->k >= 512)
+    return matmul_sharded_overlapped(ctx, site, A, B, C, m, root);
+  // B is replicated first: every rank's full B buffer receives root's.
   MAPAL_TRY(nccl_broadcast_f32(ctx, B, b_elems, root));
   for (int i = 0; i < (int)ctx->dev.size(); ++i) {
     MAPAL_TRY(enter(ctx, i));

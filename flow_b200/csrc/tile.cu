@@ -141,6 +141,13 @@ int run_site(MapalGpuCtx* ctx, int local, const MapalTileSite& s, const float* a
 
 }  // namespace
 
+int validate_tile_site(const MapalTileSite* site, const void* a, const void* b, const void* out, bool* empty,
+                       bool* matmul_shaped) {
+  MAPAL_TRY(check_site(site, a, b, out, empty));
+  *matmul_shaped = site->k > 0 && is_matmul(*site);
+  return 0;
+}
+
 int tile_site_on(MapalGpuCtx* ctx, int local, const MapalTileSite* site, const float* a, const float* b,
                  float* out, int mode) {
   bool empty = false;

@@ -354,11 +354,14 @@ def run_ours(args) -> int:
                                   max(3, min(args.steps, 10))))
     flops = 2.0 * n ** 3
     value = flops / (ms * 1e-3) / 1e12
-    # my kernels per step: whole waves of 128x128 tiles + a 64x64 remainder
-    # launch, per k-range when the B broadcast is overlapped (4 ranges)
-    tiles = -(-m // 128) * -(-n // 128)
-    full = (tiles // ctx.profile().sm_count) * ctx.profile().sm_count
-    per_pass = (1 if full else 0) + (1 if tiles > full else 0)
+    # my kernels per step: the strict site launches whole waves of 128x128
+    # tiles and, when that is estimated faster, the remainder as 64x64 tiles
+    # (launch_balanced in matmul_strict.cu); per k-range when the B broadcast
+    # is overlapped (4 ranges)
+    sms = ctx.profile().sm_count
+    waves, rem = divmod(-(-m // 128) * -(-n // 128), sms)
+    split = rem and waves + 1.35 * ((4 * rem + sms - 1) // sms) / 4 < waves + 1
+    per_pass = ((1 if waves else 0) + 1) if split else 1
     launches_per_step = per_pass * (4 if (d.world > 1 and mode == fb.STRICT) else 1)
     if mode == fb.TF32X3:
         launches_per_step = 3  # split rows, split transpose, tcgen05 GEMM

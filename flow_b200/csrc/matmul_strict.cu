@@ -256,9 +256,16 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
   const int tiles_n0 = (int)((N + 127) / 128);
   const int tiles = (int)((M + 127) / 128) * tiles_n0;
   // Whole waves of 128 x 128 CTAs (one per SM); the leftover tiles, which
-  // would run as a partly empty last wave, go as four 64 x 64 CTAs each so
-  // the last wave's work spreads over every SM.
-  const int full = (tiles / sms) * sms;
+  // would run as a partly empty last wave, may instead go as four 64 x 64
+  // CTAs each so the last wave's work spreads over every SM. A 64 x 64 CTA
+  // does a quarter of the work at about 1/kSmallCost of the per-SM rate
+  // (measured on B200), so the split is taken only when it shortens the
+  // estimated time (in units of one 128 x 128 wave).
+  constexpr double kSmallCost = 1.35;
+  const int waves = tiles / sms, rem = tiles - waves * sms;
+  const double t_full = waves + (rem ? 1.0 : 0.0);
+  const double t_split = waves + (rem ? kSmallCost * ((4 * rem + sms - 1) / sms) / 4.0 : 0.0);
+  const int full = t_split < t_full ? waves * sms : tiles;
   MAPAL_TRY((launch_cfg<128, 128, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
                                                 acc_from_c)));
   return launch_cfg<64, 64, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, full, tiles - full,

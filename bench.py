@@ -360,7 +360,7 @@ def run_ours(args) -> int:
     # is overlapped (4 ranges)
     sms = ctx.profile().sm_count
     waves, rem = divmod(-(-m // 128) * -(-n // 128), sms)
-    split = rem and waves + 1.35 * ((4 * rem + sms - 1) // sms) / 4 < waves + 1
+    split = rem > 0 and (4 * rem + sms - 1) // sms <= 2
     per_pass = ((1 if waves else 0) + 1) if split else 1
     launches_per_step = per_pass * (4 if (d.world > 1 and mode == fb.STRICT) else 1)
     if mode == fb.TF32X3:

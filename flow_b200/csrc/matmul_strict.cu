@@ -255,18 +255,18 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
                     uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed, int acc_from_c) {
   const int tiles_n0 = (int)((N + 127) / 128);
   const int tiles = (int)((M + 127) / 128) * tiles_n0;
-  // Whole waves of 128 x 128 CTAs (one per SM); the leftover tiles, which
-  // would run as a partly empty last wave, may instead go as four 64 x 64
-  // CTAs each so the last wave's work spreads over every SM. A 64 x 64 CTA
-  // does a quarter of the work at about 1/kSmallCost of the per-SM rate
-  // (measured on B200), so the split is taken only when it shortens the
-  // estimated time (in units of one 128 x 128 wave).
-  constexpr double kSmallCost = 1.35;
+  // Whole waves of 128 x 128 CTAs (one per SM). The leftover tiles would run
+  // as a partly empty last wave; when they are few (at most two 64 x 64 CTAs
+  // per SM after a four-way split) they go as 64 x 64 CTAs instead, which
+  // finish in about 0.65 of a 128 x 128 wave. Measured on B200 at
+  // N = K = 4096 for M = 256..4096: the split wins at M = 256 and 2048
+  // (a remainder of 64 and 68 tiles) and loses at 512, 1024 and 4096
+  // (128, 108 and 136 tiles), where three or four 64 x 64 CTAs per SM take
+  // longer than the partial wave.
   const int waves = tiles / sms, rem = tiles - waves * sms;
-  const double t_full = waves + (rem ? 1.0 : 0.0);
-  const double t_split = waves + (rem ? kSmallCost * ((4 * rem + sms - 1) / sms) / 4.0 : 0.0);
-  const int full = t_split < t_full ? waves * sms : tiles;
-  MAPAL_TRY((launch_cfg<128, 128, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
+  const bool split = rem > 0 && (4 * rem + sms - 1) / sms <= 2;
+  const int full = split ? waves * sms : tiles;
+  MAPAL_TRY((launch_cfg<128, 128, 32, 3, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
                                                 acc_from_c)));
   return launch_cfg<64, 64, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, full, tiles - full,
                                          tiles_n0, acc_from_c);

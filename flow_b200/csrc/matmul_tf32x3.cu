@@ -293,17 +293,29 @@ __device__ __forceinline__ void split1(float x, float& hi, float& lo) {
   lo = isfinite(hi) ? tf32_rna(__fsub_rn(x, hi)) : 0.0f;
 }
 
-// A (M x K, row stride lda) -> hi, lo (M x K, row stride kp).
+// A (M x K, row stride lda) -> hi, lo (M x K, row stride kp). Blocks walk
+// rows; threads walk a row in 16-byte groups when rows are 16-byte aligned.
 __global__ void split_rows_kernel(const float* __restrict__ A, long long lda, int M, int K, float* __restrict__ hi,
                                   float* __restrict__ lo, long long kp) {
-  const long long total = (long long)M * K;
-  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
-       e += (long long)gridDim.x * blockDim.x) {
-    const long long r = e / K, c = e % K;
-    float h, l;
-    split1(__ldg(A + r * lda + c), h, l);
-    hi[r * kp + c] = h;
-    lo[r * kp + c] = l;
+  const bool vec = (K & 3) == 0 && (lda & 3) == 0 && ((uintptr_t)A & 15) == 0;
+  for (int r = blockIdx.x; r < M; r += gridDim.x) {
+    const float* a = A + (long long)r * lda;
+    float* h = hi + (long long)r * kp;
+    float* l = lo + (long long)r * kp;
+    if (vec) {
+      for (int c = threadIdx.x; c < K / 4; c += blockDim.x) {
+        const float4 v = __ldcs(reinterpret_cast<const float4*>(a) + c);
+        float4 vh, vl;
+        split1(v.x, vh.x, vl.x);
+        split1(v.y, vh.y, vl.y);
+        split1(v.z, vh.z, vl.z);
+        split1(v.w, vh.w, vl.w);
+        reinterpret_cast<float4*>(h)[c] = vh;
+        reinterpret_cast<float4*>(l)[c] = vl;
+      }
+    } else {
+      for (int c = threadIdx.x; c < K; c += blockDim.x) split1(__ldg(a + c), h[c], l[c]);
+    }
   }
 }
 
@@ -381,7 +393,8 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   float* bhi = alo + M * kp;
   float* blo = bhi + N * kp;
   // keep every operand base 16-byte aligned (kp is a multiple of 4 floats)
-  split_rows_kernel<<<stream_grid(M * K, 256, d.prof.sm_count, 8), 256, 0, d.stream>>>(A, (long long)lda, (int)M,
+  split_rows_kernel<<<(unsigned)(M < (uint64_t)d.prof.sm_count * 8 ? M : (uint64_t)d.prof.sm_count * 8), 256, 0,
+                      d.stream>>>(A, (long long)lda, (int)M,
                                                                                         (int)K, ahi, alo, (long long)kp);
   dim3 tg((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
   if (tg.y > 65535) return set_error(MAPAL_ERR_UNSUPPORTED, "K too large for the split pass");

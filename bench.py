@@ -336,11 +336,13 @@ def run_ours(args) -> int:
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     d.barrier()
     torch.cuda.synchronize()
+    launches0 = fb.launch_count()
     for i in range(args.steps):
         flush()
         step(*evs[i])
     ctx.synchronize()
     torch.cuda.synchronize()
+    launches = fb.launch_count() - launches0  # this library's kernels in the timed region
     d.barrier()
     clk = clocks.stop()
     step_ms = [e[0].elapsed_time(e[2]) for e in evs]
@@ -354,17 +356,6 @@ def run_ours(args) -> int:
                                   max(3, min(args.steps, 10))))
     flops = 2.0 * n ** 3
     value = flops / (ms * 1e-3) / 1e12
-    # my kernels per step: the strict site launches whole waves of 128x128
-    # tiles and, when that is estimated faster, the remainder as 64x64 tiles
-    # (launch_balanced in matmul_strict.cu); per k-range when the B broadcast
-    # is overlapped (4 ranges)
-    sms = ctx.profile().sm_count
-    waves, rem = divmod(-(-m // 128) * -(-n // 128), sms)
-    split = rem > 0 and (4 * rem + sms - 1) // sms <= 2
-    per_pass = ((1 if waves else 0) + 1) if split else 1
-    launches_per_step = per_pass * (4 if (d.world > 1 and mode == fb.STRICT) else 1)
-    if mode == fb.TF32X3:
-        launches_per_step = 3  # split rows, split transpose, tcgen05 GEMM
 
     # bit-exactness spot check of this run's output (strict mode): one row
     # against the oracle is cheap; the full parity suite lives in tests/.
@@ -483,7 +474,7 @@ def run_ours(args) -> int:
                    "parallelism": f"row-shard x{d.world}, B broadcast (NCCL) inside each step",
                    "l2": "flushed between timed steps (256 MiB read)"},
         "roofline": roofline, "cpu_baseline": cb, "e2e": e2e,
-        "gpu_launches": args.steps * launches_per_step,
+        "gpu_launches": launches,
         "clocks": clk, "kernel_ms_per_step": kms, "strict_row_check": check,
         "matmul_tf32x3": tf32, "streaming": streaming,
     }

@@ -118,6 +118,11 @@ def render_f64(v: float) -> str:
     return buf.value.decode()
 
 
+def launch_count() -> int:
+    """Kernel launches libmapal_gpu has issued in this process so far."""
+    return int(lib().mapal_gpu_launch_count())
+
+
 def nccl_unique_id() -> bytes:
     buf = ctypes.create_string_buffer(128)
     _check(lib().mapal_gpu_nccl_unique_id(buf))

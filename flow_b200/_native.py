@@ -26,6 +26,7 @@ _pu64 = _c.POINTER(_c.c_uint64)
 SIGNATURES: dict[str, tuple] = {
     "mapal_gpu_abi_version": (_int, []),
     "mapal_gpu_last_error": (_c.c_char_p, []),
+    "mapal_gpu_launch_count": (_u64, []),
     "mapal_gpu_device_count": (_int, [_c.POINTER(_int)]),
     "mapal_gpu_ctx_create": (_int, [_c.c_uint32, _pp]),
     "mapal_gpu_nccl_unique_id": (_int, [_c.c_char_p]),

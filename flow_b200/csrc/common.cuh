@@ -83,6 +83,10 @@ int cuda_fail(cudaError_t e, const char* what);
     if (_rc != 0) return _rc;    \
   } while (0)
 
+// One kernel launch issued by this library (process-wide count, read by
+// mapal_gpu_launch_count).
+void count_launch();
+
 // Validate ctx and local index; make the device current.
 int enter(MapalGpuCtx* ctx, int local = 0);
 // After a launch: report launch errors; in sync mode wait and decode traps.

@@ -9,6 +9,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -29,6 +30,10 @@ int cuda_fail(cudaError_t e, const char* what) {
 
 extern "C" const char* mapal_gpu_last_error(void) { return g_last_error.c_str(); }
 extern "C" int mapal_gpu_abi_version(void) { return MAPAL_GPU_ABI_VERSION; }
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+extern "C" uint64_t mapal_gpu_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 // ---- NCCL -----------------------------------------------------------------------
 

@@ -183,12 +183,14 @@ int launch_saxpy(cudaStream_t s, int sms, float a, const float* x, const float* 
     uint64_t n4 = n / 4;
     if (n4) {
       saxpy_vec_kernel<<<stream_grid((n4 + 1) / 2, kThreads, sms, 8), kThreads, 0, s>>>(
-          a, (const float4*)x, (const float4*)y0, (float4*)y, n4);
+          a, (const float4*)x, (const float4*)y0, (float4*)y, n4); count_launch();
       done = n4 * 4;
     }
   }
-  if (done < n)
+  if (done < n) {
     saxpy_scalar_kernel<<<stream_grid(n - done, kThreads, sms, 8), kThreads, 0, s>>>(a, x, y0, y, done, n);
+    count_launch();
+  }
   return 0;
 }
 
@@ -200,13 +202,15 @@ int launch_gather(cudaStream_t s, int sms, const float* x, uint64_t n_x, const i
     uint64_t n4 = n / 4;
     if (n4) {
       gather_vec_kernel<<<stream_grid((n4 + 1) / 2, kThreads, sms, 8), kThreads, 0, s>>>(
-          x, (int64_t)n_x, (const int4*)idx, (float4*)out, n4, trap);
+          x, (int64_t)n_x, (const int4*)idx, (float4*)out, n4, trap); count_launch();
       done = n4 * 4;
     }
   }
-  if (done < n)
+  if (done < n) {
     gather_scalar_kernel<<<stream_grid(n - done, kThreads, sms, 8), kThreads, 0, s>>>(
         x, (int64_t)n_x, idx, out, done, n, trap);
+    count_launch();
+  }
   return 0;
 }
 
@@ -235,17 +239,19 @@ extern "C" int mapal_gpu_zip_map_f32(MapalGpuCtx* ctx, int op, const float* x, c
     const float4 *x4 = (const float4*)x, *y4 = (const float4*)y;
     float4* o4 = (float4*)out;
     switch (op) {
-      case MAPAL_OP_ADD: zip_vec_kernel<MAPAL_OP_ADD><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); break;
-      case MAPAL_OP_SUB: zip_vec_kernel<MAPAL_OP_SUB><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); break;
-      case MAPAL_OP_MUL: zip_vec_kernel<MAPAL_OP_MUL><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); break;
-      case MAPAL_OP_DIV: zip_vec_kernel<MAPAL_OP_DIV><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); break;
-      default: zip_vec_kernel<MAPAL_OP_MOD><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); break;
+      case MAPAL_OP_ADD: zip_vec_kernel<MAPAL_OP_ADD><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); count_launch(); break;
+      case MAPAL_OP_SUB: zip_vec_kernel<MAPAL_OP_SUB><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); count_launch(); break;
+      case MAPAL_OP_MUL: zip_vec_kernel<MAPAL_OP_MUL><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); count_launch(); break;
+      case MAPAL_OP_DIV: zip_vec_kernel<MAPAL_OP_DIV><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); count_launch(); break;
+      default: zip_vec_kernel<MAPAL_OP_MOD><<<g, kThreads, 0, d.stream>>>(x4, y4, o4, n4); count_launch(); break;
     }
     done = n4 * 4;
   }
-  if (done < n)
+  if (done < n) {
     zip_scalar_kernel<<<stream_grid(n - done, kThreads, sms, 8), kThreads, 0, d.stream>>>(op, x, y, out,
                                                                                         done, n);
+    count_launch();
+  }
   return finish(ctx, 0, false);
 }
 
@@ -278,11 +284,11 @@ extern "C" int mapal_gpu_transpose(MapalGpuCtx* ctx, const MapalMoveSite* site, 
   if (site->cq == 1) {
     dim3 grid((unsigned)((rows + kTile - 1) / kTile), (unsigned)((width + kTile - 1) / kTile));
     if (grid.y > 65535) return set_error(MAPAL_ERR_UNSUPPORTED, "transpose width too large");
-    transpose_kernel<<<grid, dim3(kTile, kRowsPerPass), 0, d.stream>>>(in, out, rows, width, site->cr);
+    transpose_kernel<<<grid, dim3(kTile, kRowsPerPass), 0, d.stream>>>(in, out, rows, width, site->cr); count_launch();
   } else {
     uint64_t n = rows * width;
     move_generic_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(
-        in, out, n, width, site->cq, site->cr);
+        in, out, n, width, site->cq, site->cr); count_launch();
   }
   return finish(ctx, 0, false);
 }

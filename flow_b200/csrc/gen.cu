@@ -78,21 +78,21 @@ constexpr int kThreads = 256;
 
 int launch_fill(cudaStream_t s, int sms, float* out, float v, uint64_t n) {
   if (n == 0) return 0;
-  fill_kernel<<<stream_grid(n, kThreads, sms, 8), kThreads, 0, s>>>(out, v, n);
+  fill_kernel<<<stream_grid(n, kThreads, sms, 8), kThreads, 0, s>>>(out, v, n); count_launch();
   return 0;
 }
 
 int launch_gen_affine(cudaStream_t s, int sms, float* out, uint64_t n, int64_t start, int32_t mul,
                       int32_t add, int32_t mod, int32_t sub) {
   if (n == 0) return 0;
-  affine_kernel<<<stream_grid(n, kThreads, sms, 8), kThreads, 0, s>>>(out, n, start, mul, add, mod, sub);
+  affine_kernel<<<stream_grid(n, kThreads, sms, 8), kThreads, 0, s>>>(out, n, start, mul, add, mod, sub); count_launch();
   return 0;
 }
 
 int launch_gen_f32(cudaStream_t s, int sms, float* out, uint64_t n, int32_t seed, int64_t offset,
                    int kind) {
   if (n == 0) return 0;
-  gen_kernel<<<stream_grid(n, kThreads, sms, 8), kThreads, 0, s>>>(out, n, seed, offset, kind);
+  gen_kernel<<<stream_grid(n, kThreads, sms, 8), kThreads, 0, s>>>(out, n, seed, offset, kind); count_launch();
   return 0;
 }
 
@@ -102,7 +102,7 @@ extern "C" int mapal_gpu_iota_i32(MapalGpuCtx* ctx, int32_t* out, uint64_t n) {
   if (n == 0) return 0;
   if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
   DeviceSlot& d = ctx->dev[0];
-  iota_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(out, n);
+  iota_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(out, n); count_launch();
   return finish(ctx, 0, false);
 }
 
@@ -111,7 +111,7 @@ extern "C" int mapal_gpu_fill_f32(MapalGpuCtx* ctx, float* out, float v, uint64_
   if (n == 0) return 0;
   if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
   DeviceSlot& d = ctx->dev[0];
-  fill_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(out, v, n);
+  fill_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(out, v, n); count_launch();
   return finish(ctx, 0, false);
 }
 
@@ -120,7 +120,7 @@ extern "C" int mapal_gpu_widen_i32_f32(MapalGpuCtx* ctx, const int32_t* in, floa
   if (n == 0) return 0;
   if (!in || !out) return set_error(MAPAL_ERR_INVALID, "null buffer");
   DeviceSlot& d = ctx->dev[0];
-  widen_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(in, out, n);
+  widen_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(in, out, n); count_launch();
   return finish(ctx, 0, false);
 }
 
@@ -155,6 +155,6 @@ extern "C" int mapal_gpu_gen_index_i32(MapalGpuCtx* ctx, int32_t* out, uint64_t 
   if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
   DeviceSlot& d = ctx->dev[0];
   gen_index_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(
-      out, n, seed, offset, range);
+      out, n, seed, offset, range); count_launch();
   return finish(ctx, 0, false);
 }

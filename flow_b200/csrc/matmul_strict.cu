@@ -74,9 +74,10 @@ struct Cfg {
   static_assert(BK % 4 == 0, "k advances in steps of 4");
 };
 
-// Work is laid out on a grid of 128 x 128 parent tiles (tiles_n0 per row of
-// tiles). A CTA of this instance covers one (128/BM)^2-th of a parent tile:
-// CTA u takes sub-tile u % split^2 of parent tile tile_base + u / split^2.
+// Work is laid out on a grid of parent tiles of 128 rows and BN*split
+// columns (tiles_n0 per row of tiles), split = 128/BM. A CTA covers one
+// split^2-th of a parent tile: CTA u takes sub-tile u % split^2 of parent
+// tile tile_base + u / split^2.
 // With acc_from_c the cells start from the values already in C (a partial
 // fold carried over from an earlier k range, bit-exact because the carried
 // accumulator is the same f32 value) instead of from the seed.
@@ -93,11 +94,11 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
   const int tid = threadIdx.x;
   const int tx = tid % G::kThreadsN, ty = tid / G::kThreadsN;
   constexpr int kSplit = 128 / BM;
-  static_assert(BM == BN && 128 % BM == 0, "square CTA tiles that divide the 128 x 128 parent tile");
+  static_assert(128 % BM == 0, "CTA rows divide the 128-row parent tile");
   const int parent = tile_base + (int)blockIdx.x / (kSplit * kSplit);
   const int sub = (int)blockIdx.x % (kSplit * kSplit);
-  const int m0 = (parent / tiles_n0) * 128 + (sub / kSplit) * BM;
-  const int n0 = (parent % tiles_n0) * 128 + (sub % kSplit) * BN;
+  const int m0 = (parent / tiles_n0) * (BM * kSplit) + (sub / kSplit) * BM;
+  const int n0 = (parent % tiles_n0) * (BN * kSplit) + (sub % kSplit) * BN;
   const int KT = (K + BK - 1) / BK;
 
   // Loader coordinates: A tile BM x BK in 16-byte groups, B tile BK x BN.
@@ -246,7 +247,7 @@ int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_
   const unsigned grid = (unsigned)ntiles * kSplit * kSplit;
   if (grid == 0) return 0;
   kern<<<grid, G::kThreads, G::kSmem, s>>>(A, B, C, (int)M, (int)N, (int)K, (long long)lda, (long long)ldb,
-                                           (long long)ldc, seed, tile_base, tiles_n0, acc_from_c);
+                                           (long long)ldc, seed, tile_base, tiles_n0, acc_from_c); count_launch();
   return 0;
 }
 
@@ -265,6 +266,18 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
   // longer than the partial wave.
   const int waves = tiles / sms, rem = tiles - waves * sms;
   const bool split = rem > 0 && (4 * rem + sms - 1) / sms <= 2;
+  // Estimated time in 128 x 128 wave units.
+  const double t_square = waves + (rem == 0 ? 0.0 : split ? 0.65 : 1.0);
+  // Alternative: 128 x 112 tiles in whole waves. A row of 37 of them spans
+  // 4144 columns, so at N = 4096 four row bands are exactly 148 tiles: the
+  // row-block sizes 512..2048 of the sharded site fill every SM. A CTA does
+  // 112/128 of a square tile's work at the same per-SM rate.
+  const int tiles_n112 = (int)((N + 111) / 112);
+  const int tiles112 = (int)((M + 127) / 128) * tiles_n112;
+  const double t_narrow = ((tiles112 + sms - 1) / sms) * (112.0 / 128.0);
+  if (t_narrow + 1e-9 < t_square)
+    return launch_cfg<128, 112, 32, 3, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, tiles112, tiles_n112,
+                                             acc_from_c);
   const int full = split ? waves * sms : tiles;
   MAPAL_TRY((launch_cfg<128, 128, 32, 3, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
                                                 acc_from_c)));

@@ -395,10 +395,10 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   // keep every operand base 16-byte aligned (kp is a multiple of 4 floats)
   split_rows_kernel<<<(unsigned)(M < (uint64_t)d.prof.sm_count * 8 ? M : (uint64_t)d.prof.sm_count * 8), 256, 0,
                       d.stream>>>(A, (long long)lda, (int)M,
-                                                                                        (int)K, ahi, alo, (long long)kp);
+                                                                                        (int)K, ahi, alo, (long long)kp); count_launch();
   dim3 tg((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
   if (tg.y > 65535) return set_error(MAPAL_ERR_UNSUPPORTED, "K too large for the split pass");
-  split_transpose_kernel<<<tg, dim3(32, 8), 0, d.stream>>>(B, (long long)ldb, (int)K, (int)N, bhi, blo, (long long)kp);
+  split_transpose_kernel<<<tg, dim3(32, 8), 0, d.stream>>>(B, (long long)ldb, (int)K, (int)N, bhi, blo, (long long)kp); count_launch();
 
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   MAPAL_TRY(make_map(&m_ahi, ahi, M, K, kp, BM));
@@ -414,6 +414,6 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   }
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
   mm_tf32x3_kernel<<<grid, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N, (int)K,
-                                                       (long long)ldc, seed, d.trap);
+                                                       (long long)ldc, seed, d.trap); count_launch();
   return 0;
 }

@@ -105,11 +105,12 @@ int launch_fold_sum(cudaStream_t s, int sms, const float* x, uint64_t n, float s
     fold_sum_kernel<true><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64);
   else
     fold_sum_kernel<false><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64);
+  count_launch();
   return 0;
 }
 
 int launch_finalize_sum(cudaStream_t s, const double* total, float seed, float* out) {
-  finalize_sum_kernel<<<1, 1, 0, s>>>(total, seed, out);
+  finalize_sum_kernel<<<1, 1, 0, s>>>(total, seed, out); count_launch();
   return 0;
 }
 

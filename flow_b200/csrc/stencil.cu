@@ -185,7 +185,7 @@ int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, ui
   }
   uint64_t blocks = (n_out + kFirTile - 1) / kFirTile;
   if (blocks > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
-  fir_kernel<<<(unsigned)blocks, kFirThreads, smem, s>>>(w, (int)taps, x, x_len, y, n_out, seed);
+  fir_kernel<<<(unsigned)blocks, kFirThreads, smem, s>>>(w, (int)taps, x, x_len, y, n_out, seed); count_launch();
   return 0;
 }
 
@@ -194,6 +194,6 @@ int launch_conv3x3(cudaStream_t s, const float* w, const float* img, uint64_t im
   dim3 grid((unsigned)((cols + kConvCols - 1) / kConvCols), (unsigned)((rows + kConvP - 1) / kConvP));
   if ((cols + kConvCols - 1) / kConvCols > 0x7fffffffull || (rows + kConvP - 1) / kConvP > 65535)
     return MAPAL_ERR_UNSUPPORTED;
-  conv3x3_kernel<<<grid, kConvThreads, 0, s>>>(w, img, img_len, stride, out, rows, cols, seed);
+  conv3x3_kernel<<<grid, kConvThreads, 0, s>>>(w, img, img_len, stride, out, rows, cols, seed); count_launch();
   return 0;
 }

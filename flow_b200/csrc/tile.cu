@@ -108,7 +108,7 @@ int launch_generic(DeviceSlot& d, const MapalTileSite& s, const float* a, const 
   const uint64_t cells = s.rows * s.c;
   tile_generic_kernel<<<stream_grid(cells, 256, d.prof.sm_count, 8), 256, 0, d.stream>>>(
       a, b, out, cells, s.c, s.k, to_generic(s.a), to_generic(s.b), s.seed, s.mul_a_first,
-      s.add_acc_first);
+      s.add_acc_first); count_launch();
   return 0;
 }
 

@@ -164,6 +164,10 @@ int mapal_gpu_abi_version(void);
 /* Message of the last error on this thread ("" if none). */
 const char* mapal_gpu_last_error(void);
 
+/* Kernel launches this library has issued in this process, all devices and
+ * contexts (a diagnostic: take the difference around a region of calls). */
+uint64_t mapal_gpu_launch_count(void);
+
 /* Number of visible CUDA devices (0 when no driver or no device). */
 int mapal_gpu_device_count(int* count);
 

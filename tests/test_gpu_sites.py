@@ -304,7 +304,9 @@ def test_matmul_known_answers(ctx, case):
 
 
 @pytest.mark.parametrize("M,N,K", [(5, 20, 7), (6, 32, 5), (33, 65, 70), (128, 128, 128), (1, 1, 1),
-                                   (257, 129, 1000), (1024, 1024, 1024), (300, 4097, 19), (127, 128, 129)])
+                                   (257, 129, 1000), (1024, 1024, 1024), (300, 4097, 19), (127, 128, 129),
+                                   # 128x112 tiling (row blocks of the sharded 4096^2 site)
+                                   (512, 4096, 64), (2048, 4096, 40), (1000, 4000, 33)])
 def test_matmul_random(ctx, M, N, K):
     A = o.gen(M * K, 0, 0)
     B = o.gen(K * N, 0, M * K)
@@ -382,6 +384,13 @@ def test_tile_site_dispatches_shapes(ctx):
     out = empty_f32(n)
     ctx.tile_site(fb.fir_site(n, 64), dev(w), dev(x), out)
     assert same_bits(host(out), o.fir(w, x, n))
+
+
+def test_launch_count_moves(ctx):
+    before = fb.launch_count()
+    C = empty_f32(64 * 64)
+    ctx.matmul(fb.matmul_site(64, 64, 64), dev(o.gen(4096, 1, 0)), dev(o.gen(4096, 1, 4096)), C)
+    assert fb.launch_count() > before
 
 
 def test_profile(ctx):

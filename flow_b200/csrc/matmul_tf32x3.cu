@@ -155,12 +155,16 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 __global__ void __launch_bounds__(kThreads, 1)
     mm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                      const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
-                     float* __restrict__ C, int M, int N, int K, long long ldc, float seed, unsigned* flag) {
+                     float* __restrict__ C, int M, int N, int K, long long ldc, float seed, unsigned* flag,
+                     int tiles_n, int tile_base, int nsplit, float* __restrict__ part_out) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  // CTA -> (tile, k part): tiles are numbered row-major over tiles_n columns.
+  const int tile = tile_base + (int)blockIdx.x / nsplit, part = (int)blockIdx.x % nsplit;
+  const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
   const int KT = (K + BK - 1) / BK;
+  const int kt_lo = (int)((long long)KT * part / nsplit), nkt = (int)((long long)KT * (part + 1) / nsplit) - kt_lo;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -186,7 +190,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     // ---- TMA producer ----
     int issued = 0;
-    for (int kt = 0; kt < KT; ++kt) {
+    for (int kt = 0; kt < nkt; ++kt) {
       const int s = kt % STAGES;
       if (kt >= STAGES && !mbar_wait(&sm.empty[s], ((kt / STAGES) - 1) & 1, abort)) {
         *abort = 1;
@@ -194,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       uint8_t* st = sm.stage[s];
       mbar_expect_tx(&sm.full[s], kStageBytes);
-      const int k0 = kt * BK;
+      const int k0 = (kt_lo + kt) * BK;
       tma_load_2d(st, &map_ahi, k0, m0, &sm.full[s]);
       tma_load_2d(st + kATile, &map_alo, k0, m0, &sm.full[s]);
       tma_load_2d(st + 2 * kATile, &map_bhi, k0, n0, &sm.full[s]);
@@ -209,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
     bool ok = true;
-    for (int kt = 0; kt < KT; ++kt) {
+    for (int kt = 0; kt < nkt; ++kt) {
       const int s = kt % STAGES;
       if (!mbar_wait(&sm.full[s], (kt / STAGES) & 1, abort)) {
         *abort = 1;
@@ -241,11 +245,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       *abort = 1;
     } else {
       const int row = m0 + quarter * 32 + lane;
+      // A k part writes its raw partial tile (row-major BM x BN) for the
+      // reduction kernel; a whole-K CTA writes C with the seed.
+      float* prow = nsplit > 1 ? part_out + (long long)blockIdx.x * (BM * BN) + (quarter * 32 + lane) * BN : nullptr;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
         tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
-        if (row < M) {
+        if (prow) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(prow + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else if (row < M) {
           float* crow = C + (long long)row * ldc + n0 + c0;
           const int nvalid = N - (n0 + c0);
           if (nvalid >= 32 && ((ldc & 3) == 0) && (((uintptr_t)C & 15) == 0)) {
@@ -274,6 +285,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// C tile (tile_base + r) = seed + sum over parts p (in order) of the partial
+// tiles part[(r * nsplit + p)], for the k-split remainder tiles. Fixed order,
+// so the result is the same on every run.
+__global__ void reduce_parts_kernel(const float* __restrict__ part, float* __restrict__ C, int M, int N,
+                                    long long ldc, float seed, int tiles_n, int tile_base, int ntiles, int nsplit) {
+  const long long total = (long long)ntiles * BM * BN;
+  for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
+       e += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(e / (BM * BN)), within = (int)(e % (BM * BN));
+    const int row = within / BN, col = within % BN;
+    const int tile = tile_base + r;
+    const int m = (tile / tiles_n) * BM + row, n = (tile % tiles_n) * BN + col;
+    if (m >= M || n >= N) continue;
+    float acc = 0.0f;
+    for (int p = 0; p < nsplit; ++p) acc += part[((long long)r * nsplit + p) * (BM * BN) + within];
+    C[(long long)m * ldc + n] = acc + seed;
   }
 }
 
@@ -387,11 +417,27 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
     return set_error(MAPAL_ERR_UNSUPPORTED, "matmul grid too large");
   const uint64_t kp = (K + 3) & ~3ull;  // TMA row strides must be multiples of 16 bytes
   const uint64_t elems = (M + N) * kp;
-  MAPAL_TRY(arena_reserve(d, 2 * elems * sizeof(float) + 4096));
+  // Tile plan: whole waves of 128 x 256 tiles; a partial last wave of R tiles
+  // is split along K into nsplit parts (R * nsplit <= SMs) whose partial
+  // tiles a reduction kernel sums in a fixed order.
+  const int sms = d.prof.sm_count;
+  const int tiles_n = (int)((N + BN - 1) / BN);
+  const int tiles = (int)((M + BM - 1) / BM) * tiles_n;
+  const int KT = (int)((K + BK - 1) / BK);
+  const int full = (tiles / sms) * sms, rem = tiles - full;
+  int nsplit = 1;
+  if (rem > 0 && rem <= sms / 2) {
+    nsplit = sms / rem;
+    if (nsplit > 4) nsplit = 4;
+    if (nsplit > KT) nsplit = KT;
+  }
+  const uint64_t part_elems = nsplit > 1 ? (uint64_t)rem * nsplit * BM * BN : 0;
+  MAPAL_TRY(arena_reserve(d, (2 * elems + part_elems) * sizeof(float) + 4096));
   float* ahi = (float*)d.arena;
   float* alo = ahi + M * kp;
   float* bhi = alo + M * kp;
   float* blo = bhi + N * kp;
+  float* parts = blo + N * kp;
   // keep every operand base 16-byte aligned (kp is a multiple of 4 floats)
   split_rows_kernel<<<(unsigned)(M < (uint64_t)d.prof.sm_count * 8 ? M : (uint64_t)d.prof.sm_count * 8), 256, 0,
                       d.stream>>>(A, (long long)lda, (int)M,
@@ -412,8 +458,23 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
     MAPAL_CUDA(cudaFuncSetAttribute(mm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set |= 1ull << d.device;
   }
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  mm_tf32x3_kernel<<<grid, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N, (int)K,
-                                                       (long long)ldc, seed, d.trap); count_launch();
+  const int whole = nsplit > 1 ? full : tiles;  // tiles computed over all of K
+  if (whole > 0) {
+    mm_tf32x3_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N,
+                                                                    (int)K, (long long)ldc, seed, d.trap, tiles_n, 0,
+                                                                    1, nullptr);
+    count_launch();
+  }
+  if (nsplit > 1) {
+    mm_tf32x3_kernel<<<(unsigned)(rem * nsplit), kThreads, smem, d.stream>>>(
+        m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_n, full, nsplit,
+        parts);
+    count_launch();
+    const uint64_t n_red = (uint64_t)rem * BM * BN;
+    reduce_parts_kernel<<<stream_grid(n_red, 256, sms, 8), 256, 0, d.stream>>>(parts, C, (int)M, (int)N,
+                                                                              (long long)ldc, seed, tiles_n, full,
+                                                                              rem, nsplit);
+    count_launch();
+  }
   return 0;
 }

@@ -46,18 +46,20 @@ __global__ void __launch_bounds__(kThreads) fold_sum_kernel(const float* __restr
     const float4* x4 = reinterpret_cast<const float4*>(x);
     const uint64_t n4 = n / 4;
     uint64_t i = gid;
-    for (; i + stride < n4; i += 2 * stride) {
-      float4 a = __ldcs(x4 + i), b = __ldcs(x4 + i + stride);
-      acc += (double)a.x;
-      acc += (double)a.y;
-      acc += (double)a.z;
-      acc += (double)a.w;
-      acc += (double)b.x;
-      acc += (double)b.y;
-      acc += (double)b.z;
-      acc += (double)b.w;
+    // Four 16-byte loads in flight per thread per trip.
+    for (; i + 3 * stride < n4; i += 4 * stride) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcs(x4 + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc += (double)v[u].x;
+        acc += (double)v[u].y;
+        acc += (double)v[u].z;
+        acc += (double)v[u].w;
+      }
     }
-    if (i < n4) {
+    for (; i < n4; i += stride) {
       float4 a = __ldcs(x4 + i);
       acc += (double)a.x;
       acc += (double)a.y;

@@ -454,6 +454,13 @@ def run_ours(args) -> int:
     if not args.no_streaming:
         streaming = run_streaming(ctx, d, fb, torch, flush, pk)
 
+    big_mm = None
+    if not args.no_16384:
+        # free the 4096^2 operands first
+        del A, B, C
+        torch.cuda.empty_cache()
+        big_mm = run_matmul_16384(ctx, d, fb, torch, pk)
+
     cb = None
     if d.rank == 0 and d.world == 1 and not args.no_cpu:
         try:
@@ -476,13 +483,52 @@ def run_ours(args) -> int:
         "roofline": roofline, "cpu_baseline": cb, "e2e": e2e,
         "gpu_launches": launches,
         "clocks": clk, "kernel_ms_per_step": kms, "strict_row_check": check,
-        "matmul_tf32x3": tf32, "streaming": streaming,
+        "matmul_tf32x3": tf32, "streaming": streaming, "matmul_16384": big_mm,
     }
     if d.rank == 0:
         emit_line(line)
     ctx.close()
     d.close()
     return 0
+
+
+def run_matmul_16384(ctx, d, fb, torch, pk) -> dict:
+    """The 16384^2 row-sharded matmul: A, B uniform[-1,1)
+    from seed 4, A row blocks per rank, B broadcast from rank 0 inside every
+    step; strict and 3xTF32, 1 warm-up + 2 timed steps each (inputs are 1 GiB
+    each, far beyond L2)."""
+    n = 16384
+    lo, hi = fb.shard_range(n, d.world, d.rank)
+    m = hi - lo
+    A = torch.empty(m * n, dtype=torch.float32, device="cuda")
+    B = torch.empty(n * n, dtype=torch.float32, device="cuda")
+    C = torch.empty(max(m, 1) * n, dtype=torch.float32, device="cuda")
+    ctx.gen(A, 4, lo * n)
+    ctx.gen(B, 4, n * n)
+    ctx.synchronize()
+    site = fb.matmul_site(n, n, n)
+    stream = torch.cuda.current_stream()
+    out = {"workload": "f32 matmul M=N=K=16384, row blocks per rank, B broadcast (NCCL) in each step",
+           "data": "uniform[-1,1) from seed 4"}
+    sms = ctx.profile().sm_count
+    for name, mode in (("strict", fb.STRICT), ("tf32x3", fb.TF32X3)):
+        def step():
+            if d.world > 1:
+                ctx.matmul_sharded(site, [A], [B], [C], [m], root=0, mode=mode)
+            else:
+                ctx.matmul(site, A, B, C, mode)
+        ms = d.max(time_launches(torch, stream, step, lambda: None, 2))
+        tf = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
+        r = {"ms_per_step": ms, "value": tf, "unit": "TFLOP/s", "per_gpu": tf / d.world}
+        if mode == fb.STRICT:
+            r["frac_per_gpu"] = tf / d.world / (sms * 128 * pk["sm_max_mhz"] * 1e6 / 1e12)
+        else:
+            r["frac_per_gpu_of_tf32_div3"] = 3 * tf / d.world / (pk["bf16_tflops"] / 2.0)
+        out[name] = r
+    ctx.synchronize()
+    del A, B, C
+    torch.cuda.empty_cache()
+    return out
 
 
 def time_launches(torch, stream, fn, flush, reps: int) -> float:
@@ -576,6 +622,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--no-tf32", action="store_true", help="skip the opt-in 3xTF32 measurement")
+    ap.add_argument("--no-16384", action="store_true", help="skip the 16384^2 sharded matmul lines")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--mode", choices=["strict", "tf32x3"], default="strict")
     ap.add_argument("--no-streaming", action="store_true")

@@ -21,7 +21,8 @@ import ctypes
 from typing import Sequence
 
 from . import _native
-from .records import GpuProfile, KSplit, MoveSite, TileRead, TileSite, conv2d_site, fir_site, matmul_site, transpose_site
+from .records import (ExprOp, GpuProfile, KSplit, MoveSite, TileRead, TileSite, conv2d_site, fir_site,
+                      matmul_site, program, transpose_site)
 
 __all__ = [
     "Context", "MapalTrap", "MapalInfraError", "Unsupported", "TileSite", "TileRead", "KSplit",
@@ -235,6 +236,13 @@ class Context:
 
     def zip_map(self, op: int, x, y, out) -> None:
         _check(lib().mapal_gpu_zip_map_f32(self._h, op, _ptr(x), _ptr(y), _ptr(out), out.numel()))
+
+    def map_expr(self, prog, arrays, out, n: int | None = None) -> None:
+        """out[t] = prog evaluated at element t (see records.program)."""
+        n = out.numel() if n is None else n
+        lens = _u64s([a.numel() for a in arrays]) if arrays else None
+        _check(lib().mapal_gpu_map_expr(self._h, prog, len(prog), _arr(arrays) if arrays else None, lens,
+                                        len(arrays), _ptr(out), n))
 
     def transpose(self, site: MoveSite, inp, out) -> None:
         _check(lib().mapal_gpu_transpose(self._h, ctypes.byref(site), _ptr(inp), _ptr(out)))

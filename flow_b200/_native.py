@@ -8,7 +8,7 @@ from __future__ import annotations
 import ctypes
 import os
 
-from .records import GpuProfile, MoveSite, TileSite
+from .records import ExprOp, GpuProfile, MoveSite, TileSite
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libmapal_gpu.so")
 
@@ -47,6 +47,7 @@ SIGNATURES: dict[str, tuple] = {
     "mapal_gpu_gen_index_i32": (_int, [_vp, _vp, _u64, _i32, _i64, _i32]),
     "mapal_gpu_map_saxpy": (_int, [_vp, _f32, _vp, _vp, _vp, _u64]),
     "mapal_gpu_zip_map_f32": (_int, [_vp, _int, _vp, _vp, _vp, _u64]),
+    "mapal_gpu_map_expr": (_int, [_vp, _c.POINTER(ExprOp), _c.c_uint32, _pp, _pu64, _c.c_uint32, _vp, _u64]),
     "mapal_gpu_transpose": (_int, [_vp, _c.POINTER(MoveSite), _vp, _vp]),
     "mapal_gpu_gather": (_int, [_vp, _vp, _u64, _vp, _vp, _u64]),
     "mapal_gpu_fold_sum_f32": (_int, [_vp, _f32, _vp, _u64, _vp]),

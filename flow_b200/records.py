@@ -54,6 +54,35 @@ class MoveSite(ctypes.Structure):
     ]
 
 
+class ExprOp(ctypes.Structure):
+    """One op of a general map body (MAPAL_X_* in include/mapal_gpu.h)."""
+    _fields_ = [("code", ctypes.c_uint16), ("slot", ctypes.c_uint16), ("i", ctypes.c_int32),
+                ("f", ctypes.c_float)]
+
+
+# MAPAL_X_* op codes
+X = dict(T_I32=0, CONST_I32=1, CONST_F32=2, IN_I32=3, IN_F32=4, LOAD_I32=5, LOAD_F32=6, ADD_I32=10,
+         SUB_I32=11, MUL_I32=12, DIV_I32=13, REM_I32=14, NEG_I32=15, ADD_F32=20, SUB_F32=21, MUL_F32=22,
+         DIV_F32=23, REM_F32=24, NEG_F32=25, WIDEN_I32_F32=30, STORE_I32=40, STORE_F32=41)
+
+
+def program(*ops) -> ctypes.Array:
+    """Build an ExprOp array from (name[, slot | imm]) tuples, e.g.
+    program(("T_I32",), ("CONST_I32", 7), ("MUL_I32",), ("WIDEN_I32_F32",), ("STORE_F32",))."""
+    arr = (ExprOp * len(ops))()
+    for k, op in enumerate(ops):
+        name = op[0]
+        arr[k].code = X[name]
+        if len(op) > 1:
+            if name in ("IN_I32", "IN_F32", "LOAD_I32", "LOAD_F32"):
+                arr[k].slot = op[1]
+            elif name == "CONST_F32":
+                arr[k].f = op[1]
+            else:
+                arr[k].i = op[1]
+    return arr
+
+
 class GpuProfile(ctypes.Structure):
     """Machine facts (the sm_100a counterpart of profile.rs:99-156 Machine::Gpu)."""
     _fields_ = [

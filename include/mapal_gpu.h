@@ -250,6 +250,58 @@ int mapal_gpu_map_saxpy(MapalGpuCtx* ctx, float a, const float* x, const float* 
 int mapal_gpu_zip_map_f32(MapalGpuCtx* ctx, int op, const float* x, const float* y, float* out,
                           uint64_t n);
 
+/* General map body, for Map sites whose element body is scalar arithmetic
+ * (Map eval.rs:297-324 with the element ops of eval.rs:544-596; the rung-0
+ * map kernels kernel.rs:1156-1333 cover the same ground with generated code).
+ * out[t] for t in [0, n) is the value a stack program leaves, evaluated per
+ * element over 32-bit values:
+ *   T_I32            push t (the element index, < 2^31)
+ *   CONST_I32/F32    push the immediate i / f
+ *   IN_I32/F32 s     push arrays[s][t]   (the mapped or zipped inputs)
+ *   LOAD_I32/F32 s   pop an i32 index j, push arrays[s][j]; j outside
+ *                    [0, lens[s]) traps index_oob (the Index rule)
+ *   ADD/SUB/MUL/DIV/REM/NEG _I32   wrapping i32; DIV and REM by zero trap
+ *                    div_zero, MIN / -1 wraps, % takes the dividend's sign
+ *   ADD/SUB/MUL/DIV/REM/NEG _F32   IEEE binary32, each op rounded (REM = fmodf)
+ *   WIDEN_I32_F32    convert to f32, round to nearest
+ *   STORE_I32/F32    pop the result; must be the last op
+ * The program is checked on the host (types, stack depth <= 16, slots,
+ * at most 64 ops) and rejected with MAPAL_ERR_INVALID if malformed. */
+#define MAPAL_X_T_I32 0
+#define MAPAL_X_CONST_I32 1
+#define MAPAL_X_CONST_F32 2
+#define MAPAL_X_IN_I32 3
+#define MAPAL_X_IN_F32 4
+#define MAPAL_X_LOAD_I32 5
+#define MAPAL_X_LOAD_F32 6
+#define MAPAL_X_ADD_I32 10
+#define MAPAL_X_SUB_I32 11
+#define MAPAL_X_MUL_I32 12
+#define MAPAL_X_DIV_I32 13
+#define MAPAL_X_REM_I32 14
+#define MAPAL_X_NEG_I32 15
+#define MAPAL_X_ADD_F32 20
+#define MAPAL_X_SUB_F32 21
+#define MAPAL_X_MUL_F32 22
+#define MAPAL_X_DIV_F32 23
+#define MAPAL_X_REM_F32 24
+#define MAPAL_X_NEG_F32 25
+#define MAPAL_X_WIDEN_I32_F32 30
+#define MAPAL_X_STORE_I32 40
+#define MAPAL_X_STORE_F32 41
+#define MAPAL_X_MAX_OPS 64
+#define MAPAL_X_MAX_ARRAYS 8
+
+typedef struct MapalExprOp {
+  uint16_t code;
+  uint16_t slot;
+  int32_t i;
+  float f;
+} MapalExprOp;
+
+int mapal_gpu_map_expr(MapalGpuCtx* ctx, const MapalExprOp* prog, uint32_t nops, const void* const* arrays,
+                       const uint64_t* lens, uint32_t narrays, void* out, uint64_t n);
+
 /* Move site (transpose and other affine permutations),
  * benches/shapes/transpose_1024.mapal:11; MoveSite algo.rs:309-333. */
 int mapal_gpu_transpose(MapalGpuCtx* ctx, const MapalMoveSite* site, const float* in,

@@ -284,3 +284,24 @@ def transpose_site(R: int, C: int) -> MoveSite:
     s = MoveSite()
     s.width, s.rows, s.cq, s.cr, s.len = R, C, 1, C, R * C
     return s
+
+
+class ExprOp(ctypes.Structure):
+    """MAPAL_X_* op (include/mapal_gpu.h)."""
+    _fields_ = [("code", ctypes.c_uint16), ("slot", ctypes.c_uint16), ("i", ctypes.c_int32),
+                ("f", ctypes.c_float)]
+
+
+def map_expr(prog, arrays: list, n: int, out_dtype=np.float32):
+    """Evaluate a map-body program over [0, n): (rc, out)."""
+    L = lib()
+    L.or_map_expr.argtypes = [ctypes.POINTER(ExprOp), ctypes.c_uint32, ctypes.POINTER(ctypes.c_void_p),
+                              ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint32, ctypes.c_void_p, ctypes.c_uint64]
+    ops = (ExprOp * len(prog))()
+    for k, p in enumerate(prog):
+        ops[k].code, ops[k].slot, ops[k].i, ops[k].f = p.code, p.slot, p.i, p.f
+    ptrs = (ctypes.c_void_p * max(1, len(arrays)))(*[a.ctypes.data for a in arrays])
+    lens = (ctypes.c_uint64 * max(1, len(arrays)))(*[a.size for a in arrays])
+    out = np.zeros(n, out_dtype)
+    rc = L.or_map_expr(ops, len(prog), ptrs, lens, len(arrays), out.ctypes.data, n)
+    return rc, out

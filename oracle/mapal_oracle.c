@@ -298,6 +298,75 @@ void or_conv2d_3x3(const float* w, const float* img, int64_t stride, float* out,
     }
 }
 
+/* ---- general map body: Map eval.rs:297-324, arith eval.rs:544-596 ---------------- */
+
+static uint32_t fbits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  return u;
+}
+
+static float bitsf(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+int or_map_expr(const MapalExprOp* prog, uint32_t nops, const void* const* arrays, const uint64_t* lens,
+                uint32_t narrays, void* out, uint64_t n) {
+  (void)narrays;
+  for (uint64_t t = 0; t < n; ++t) {
+    uint32_t st[16];
+    int sp = 0;
+    for (uint32_t pc = 0; pc < nops; ++pc) {
+      const MapalExprOp* op = &prog[pc];
+      switch (op->code) {
+        case MAPAL_X_T_I32: st[sp++] = (uint32_t)t; break;
+        case MAPAL_X_CONST_I32: st[sp++] = (uint32_t)op->i; break;
+        case MAPAL_X_CONST_F32: st[sp++] = fbits(op->f); break;
+        case MAPAL_X_IN_I32:
+        case MAPAL_X_IN_F32: st[sp++] = ((const uint32_t*)arrays[op->slot])[t]; break;
+        case MAPAL_X_LOAD_I32:
+        case MAPAL_X_LOAD_F32: {
+          int64_t j = (int64_t)(int32_t)st[sp - 1];
+          if (j < 0 || (uint64_t)j >= lens[op->slot]) return MAPAL_TRAP_INDEX_OOB;
+          st[sp - 1] = ((const uint32_t*)arrays[op->slot])[j];
+          break;
+        }
+        case MAPAL_X_NEG_I32: st[sp - 1] = (uint32_t)or_i32_sub(0, (int32_t)st[sp - 1]); break;
+        case MAPAL_X_NEG_F32: st[sp - 1] = fbits(-bitsf(st[sp - 1])); break;
+        case MAPAL_X_WIDEN_I32_F32: st[sp - 1] = fbits((float)(int32_t)st[sp - 1]); break;
+        case MAPAL_X_STORE_I32:
+        case MAPAL_X_STORE_F32: ((uint32_t*)out)[t] = st[--sp]; break;
+        default: {
+          uint32_t b = st[--sp], a = st[sp - 1];
+          int32_t r32;
+          switch (op->code) {
+            case MAPAL_X_ADD_I32: st[sp - 1] = (uint32_t)or_i32_add((int32_t)a, (int32_t)b); break;
+            case MAPAL_X_SUB_I32: st[sp - 1] = (uint32_t)or_i32_sub((int32_t)a, (int32_t)b); break;
+            case MAPAL_X_MUL_I32: st[sp - 1] = (uint32_t)or_i32_mul((int32_t)a, (int32_t)b); break;
+            case MAPAL_X_DIV_I32:
+              if (or_i32_div((int32_t)a, (int32_t)b, &r32)) return MAPAL_TRAP_DIV_ZERO;
+              st[sp - 1] = (uint32_t)r32;
+              break;
+            case MAPAL_X_REM_I32:
+              if (or_i32_rem((int32_t)a, (int32_t)b, &r32)) return MAPAL_TRAP_DIV_ZERO;
+              st[sp - 1] = (uint32_t)r32;
+              break;
+            case MAPAL_X_ADD_F32: st[sp - 1] = fbits(bitsf(a) + bitsf(b)); break;
+            case MAPAL_X_SUB_F32: st[sp - 1] = fbits(bitsf(a) - bitsf(b)); break;
+            case MAPAL_X_MUL_F32: st[sp - 1] = fbits(bitsf(a) * bitsf(b)); break;
+            case MAPAL_X_DIV_F32: st[sp - 1] = fbits(bitsf(a) / bitsf(b)); break;
+            case MAPAL_X_REM_F32: st[sp - 1] = fbits(fmodf(bitsf(a), bitsf(b))); break;
+            default: return MAPAL_ERR_INVALID;
+          }
+        }
+      }
+    }
+  }
+  return 0;
+}
+
 /* ---- Rust Display of floats: value.rs:90-100 ------------------------------------ */
 
 /* Shortest digit string d (p digits, decimal exponent e: value = d.ddd x 10^e)

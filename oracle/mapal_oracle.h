@@ -97,6 +97,14 @@ void or_fir(const float* w, int64_t taps, const float* x, float* y, int64_t n_ou
 void or_conv2d_3x3(const float* w, const float* img, int64_t stride, float* out,
                    int64_t out_rows, int64_t out_cols);
 
+/* A map body given as a MAPAL_X_* stack program (include/mapal_gpu.h),
+ * evaluated element by element in order (Map eval.rs:297-324; arithmetic
+ * eval.rs:544-596). out holds 32-bit values (i32 or f32 bits). Returns 0, or
+ * the trap of the first element that traps (MAPAL_TRAP_DIV_ZERO /
+ * MAPAL_TRAP_INDEX_OOB); elements before it are written. */
+int or_map_expr(const MapalExprOp* prog, uint32_t nops, const void* const* arrays, const uint64_t* lens,
+                uint32_t narrays, void* out, uint64_t n);
+
 /* Rust `Display` of an f32 / f64 (value.rs:90-100): shortest round-trip
  * digits, positional notation, "NaN", "inf", "-inf", "-0". Returns length. */
 int or_render_f32(float v, char* buf, int cap);

@@ -23,6 +23,8 @@ CSRC = os.path.join(HERE, "csrc")
 BUILD = os.path.join(HERE, "_build")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 LIB = os.path.join(HERE, "libmapal_gpu.so")
+DRIVER_SRC = os.path.join(HERE, "driver", "mapal_run.cpp")
+DRIVER = os.path.join(HERE, "mapal-run")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # -fmad=false: no multiply and add is ever contracted into an FMA (the
@@ -83,9 +85,29 @@ def build(force: bool = False, verbose: bool = False) -> str:
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    build_driver(force)
     if verbose:
         print(LIB)
+        print(DRIVER)
     return LIB
+
+
+def build_driver(force: bool = False) -> str:
+    """Link the program driver (flow_b200/mapal-run) against the library.
+
+    The CUDA runtime is linked statically; the library is found next to the
+    binary through its rpath."""
+    newest = max(os.path.getmtime(DRIVER_SRC), os.path.getmtime(LIB), _headers_mtime())
+    if force or not os.path.exists(DRIVER) or os.path.getmtime(DRIVER) < newest:
+        cuda = os.path.dirname(os.path.dirname(nvcc()))
+        cmd = ["g++", "-O2", "-std=c++17", "-ffp-contract=off", "-I", INCLUDE, "-I",
+               os.path.join(cuda, "include"), DRIVER_SRC, "-o", DRIVER, "-L", HERE, "-lmapal_gpu",
+               "-L", os.path.join(cuda, "lib64"), "-lcudart_static", "-ldl", "-lrt", "-lpthread",
+               "-Wl,-rpath,$ORIGIN"]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"driver link failed: {' '.join(cmd)}\n{r.stdout}\n{r.stderr}")
+    return DRIVER
 
 
 def main() -> int:

@@ -1,0 +1,136 @@
+"""The program driver without a GPU: the oracle's program evaluator pinned to the
+reference's known answers, and the driver's site plan for each program.
+
+`mapal-run --plan` reads a program and prints the ABI calls it would make
+(no device needed); programs outside the subset exit 2.
+"""
+import glob
+import json
+import os
+import subprocess
+
+import pytest
+
+import mapal_programs as P
+from oracle.mapal_eval import TIME_MARK, expected, matches
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+DRIVER = os.path.join(ROOT, "flow_b200", "mapal-run")
+PROGRAMS = sorted(glob.glob(os.path.join(HERE, "programs", "*.mapal")))
+GOLD = json.load(open(os.path.join(HERE, "golden", "reference_outputs.json")))
+
+
+def _gold(table, shape, size):
+    for c in GOLD[table]:
+        if c["shape"] == shape and c["size"] == size:
+            return c["values"]
+    raise KeyError((shape, size))
+
+
+# ---- the evaluator against the reference's known answers ---------------------------
+
+@pytest.mark.parametrize("case", [c for c in GOLD["matmul_known_answers"] if c["n"] <= 256],
+                         ids=lambda c: f"n{c['n']}")
+def test_eval_matmul_known_answers(case):
+    out, rc = expected(P.matmul(case["n"]))
+    assert rc == 0 and out == f"{case['c0']}\n{case['clast']}\n"
+
+
+@pytest.mark.parametrize("shape,size,prog", [
+    ("saxpy", 256, P.saxpy), ("saxpy", 1048576, P.saxpy), ("reduce", 256, P.reduce),
+    ("reduce", 1048576, P.reduce), ("transpose", 16, P.transpose), ("transpose", 1024, P.transpose),
+    ("gather", 256, P.gather), ("gather", 1048576, P.gather)])
+def test_eval_matches_ladder2(shape, size, prog):
+    out, rc = expected(prog(size))
+    assert rc == 0 and out.split("\n")[:-1] == _gold("ladder2", shape, size)
+
+
+@pytest.mark.parametrize("shape,size", [("fir", 256), ("fir", 65536), ("conv2d", 16), ("conv2d", 20),
+                                        ("conv2d", 92), ("conv2d", 512)])
+def test_eval_matches_shapes_baseline(shape, size):
+    out, rc = expected(P.fir(size) if shape == "fir" else P.conv2d(size))
+    assert rc == 0 and out.split("\n")[:-1] == _gold("shapes", shape, size)
+
+
+def test_eval_float_print_pin():
+    out, rc = expected(P.FLOAT_PRINT)
+    assert rc == 0 and out.split("\n")[:-1] == GOLD["float_print_pin"]["lines"]
+
+
+def test_eval_traps_and_order():
+    # the print before the trapping site appears, nothing after it
+    src = 'fn main() {\n 10 -> iota -> d;\n "a" -> println;\n d -> map { i -> 5 / (i - 3) } -> q;\n' \
+          ' "b" -> println;\n}\n'
+    assert expected(src) == ("a\n", 101)
+    src = "fn main() {\n 4 -> iota -> d;\n d -> map { i -> i + 1 } -> e;\n d -> map { i -> d[i] } -> ok;\n" \
+          " e -> map { j -> ok[j] } -> bad;\n}\n"
+    assert expected(src)[1] == 101
+
+
+def test_time_mark_matching():
+    assert matches("ms=1.25\n", "ms=" + TIME_MARK + "\n")
+    assert matches("ms=3\n", "ms=" + TIME_MARK + "\n")
+    assert not matches("ms=1.25\nx\n", "ms=" + TIME_MARK + "\n")
+
+
+# ---- the driver's site plan ---------------------------------------------------------
+
+def _plan(src: str, tmp_path) -> subprocess.CompletedProcess:
+    f = tmp_path / "p.mapal"
+    f.write_text(src)
+    return subprocess.run([DRIVER, "--plan", str(f)], capture_output=True, text=True, timeout=60)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _driver_built():
+    if not os.path.exists(DRIVER):
+        pytest.fail(f"{DRIVER} is missing: python -m flow_b200.build")
+
+
+@pytest.mark.parametrize("prog,site", [
+    (P.matmul(64), "tile_site rows=64 c=64 k=64 a{base=0 ci=64 ck=1 clane=0 ks=0/0/0} "
+                   "b{base=0 ci=0 ck=64 clane=1 ks=0/0/0}"),
+    (P.fir(1000, 17), "tile_site rows=1 c=1000 k=17 a{base=0 ci=0 ck=1 clane=0 ks=0/0/0} "
+                      "b{base=0 ci=0 ck=1 clane=1 ks=0/0/0}"),
+    (P.conv2d(30), "tile_site rows=30 c=30 k=9 a{base=0 ci=0 ck=1 clane=0 ks=0/0/0} "
+                   "b{base=0 ci=32 ck=0 clane=1 ks=3/32/1}"),
+    (P.saxpy(1000), "saxpy n=1000"),
+    (P.reduce(1000), "fold_sum_f32 n=1000"),
+    (P.transpose(40), "move_site width=40 rows=40 cq=1 cr=40"),
+    (P.gather(1000), "gather n=1000 n_x=1000"),
+])
+def test_plan_recognises_sites(prog, site, tmp_path):
+    r = _plan(prog, tmp_path)
+    assert r.returncode == 0, r.stderr
+    assert site in r.stdout.split("\n")
+
+
+@pytest.mark.parametrize("path", PROGRAMS, ids=os.path.basename)
+def test_plan_every_program(path):
+    r = subprocess.run([DRIVER, "--plan", path], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    # a program with bulk statements makes ABI calls
+    calls = [ln for ln in r.stdout.split("\n") if ln and not ln.startswith(("print", "read element"))]
+    assert bool(calls) == ("-> map" in open(path).read())
+
+
+def test_plan_general_body_uses_map_expr(tmp_path):
+    r = _plan("fn main() {\n 100 -> iota -> d;\n d -> map { i -> i * i % 7 -> widen_f32 } -> f;\n"
+              " f -> map { x -> x / 3.0 - x % 2.0 } -> g;\n g[5] -> println;\n}\n", tmp_path)
+    assert r.returncode == 0, r.stderr
+    assert "map_expr n=100 ops=7 arrays=0" in r.stdout  # i, i, *, 7, %, widen, store
+    assert "map_expr n=100 ops=8 arrays=1" in r.stdout
+
+
+@pytest.mark.parametrize("src,why", [
+    ("fn helper() { 1 -> println; }\nfn main() { 1 -> println; }\n", "functions other than main"),
+    ("fn main() {\n mut k: i32 <- 0;\n}\n", "expected"),
+    ("fn main() {\n 10 -> iota -> d;\n d -> map { i -> i -> widen_f64 } -> e;\n}\n", "map body stage"),
+    ("fn main() {\n 10 -> iota -> d;\n d -> map { i -> (1, d) -> fold { a, v -> a * v } } -> e;\n}\n",
+     "fold"),
+])
+def test_plan_refuses_outside_subset(src, why, tmp_path):
+    r = _plan(src, tmp_path)
+    assert r.returncode == 2
+    assert "unsupported" in r.stderr and why in r.stderr

@@ -1,0 +1,57 @@
+"""The program driver on the GPU: `mapal-run prog.mapal` against the oracle's
+program evaluator — the same stdout byte for byte and the same exit code
+(0, or 101 after a trap), the protocol of the reference's CUDA differential
+tests (crates/backends/cuda/tests/differential.rs:242-276)."""
+import glob
+import os
+import subprocess
+
+import pytest
+
+import mapal_programs as P
+from oracle.mapal_eval import expected, matches
+
+pytestmark = pytest.mark.gpu
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+DRIVER = os.path.join(os.path.dirname(HERE), "flow_b200", "mapal-run")
+PROGRAMS = sorted(glob.glob(os.path.join(HERE, "programs", "*.mapal")))
+
+
+def _run(path: str) -> subprocess.CompletedProcess:
+    return subprocess.run([DRIVER, path], capture_output=True, text=True, timeout=300)
+
+
+def _check(path: str, src: str):
+    want, want_rc = expected(src)
+    r = _run(path)
+    assert r.returncode == want_rc, (r.returncode, r.stdout, r.stderr)
+    assert matches(r.stdout, want), (r.stdout, want)
+    if want_rc == 101:
+        assert r.stderr.startswith("mapal trap: ")
+
+
+@pytest.mark.parametrize("path", PROGRAMS, ids=os.path.basename)
+def test_program(path):
+    _check(path, open(path).read())
+
+
+@pytest.mark.parametrize("name,src", [
+    ("saxpy_2e20", P.saxpy(1 << 20)), ("reduce_2e20", P.reduce(1 << 20)),
+    ("transpose_1024", P.transpose(1024)), ("gather_2e20", P.gather(1 << 20)),
+    ("fir_2e20", P.fir(1 << 20)), ("conv2d_1024", P.conv2d(1024)), ("matmul_256", P.matmul(256)),
+    ("float_print", P.FLOAT_PRINT)])
+def test_bench_shape(name, src, tmp_path):
+    f = tmp_path / f"{name}.mapal"
+    f.write_text(src)
+    _check(str(f), src)
+
+
+def test_matmul_4096_known_answer(tmp_path):
+    # the headline shape end to end: c[0] and c[N*N-1] of the integer-generator
+    # product are the reference's published known answers
+    f = tmp_path / "matmul_4096.mapal"
+    f.write_text(P.matmul(4096))
+    r = _run(str(f))
+    assert r.returncode == 0, r.stderr
+    assert r.stdout == "74348\n-302529\n"

@@ -11,6 +11,7 @@
 // per-block partials in a fixed order. The shape of the tree depends only on
 // n and the SM count, so the result is the same on every run.
 #include "common.cuh"
+#include "cpasync.cuh"
 
 namespace {
 
@@ -111,6 +112,72 @@ int launch_fold_sum(cudaStream_t s, int sms, const float* x, uint64_t n, float s
   return 0;
 }
 
+namespace {
+
+// The strict left fold: the block's threads stage chunks of x into a shared
+// ring with cp.async, thread 0 adds them in order. The ring hides the load
+// latency, leaving the chain of dependent adds as the only cost.
+constexpr int kStrictThreads = 256;
+constexpr int kStrictChunk = 2048;  // floats per stage
+constexpr int kStrictStages = 4;
+
+template <bool kAligned>
+__global__ void __launch_bounds__(kStrictThreads) fold_sum_strict_kernel(const float* __restrict__ x,
+                                                                         uint64_t n, float seed,
+                                                                         float* out) {
+  __shared__ __align__(16) float ring[kStrictStages][kStrictChunk];
+  const uint64_t chunks = (n + kStrictChunk - 1) / kStrictChunk;
+  auto issue = [&](uint64_t c) {
+    if (c < chunks) {
+      const uint64_t base = c * kStrictChunk;
+      float* buf = ring[c % kStrictStages];
+      for (int g = threadIdx.x; g < kStrictChunk / 4; g += kStrictThreads) {
+        const uint64_t e = base + 4 * (uint64_t)g;
+        const int64_t left = (int64_t)n - (int64_t)e;
+        const int nvalid = left >= 4 ? 4 : (left > 0 ? (int)left : 0);
+        copy4(smem_u32(buf + 4 * g), x + (nvalid ? e : 0), nvalid, kAligned);
+      }
+    }
+    cp_commit();  // an empty group keeps the wait count uniform
+  };
+#pragma unroll
+  for (int s = 0; s < kStrictStages - 1; ++s) issue(s);
+  float acc = seed;
+  for (uint64_t c = 0; c < chunks; ++c) {
+    cp_wait<kStrictStages - 2>();
+    __syncthreads();  // chunk c landed for every thread; chunk c-1's buffer is free
+    issue(c + kStrictStages - 1);
+    if (threadIdx.x == 0) {
+      const float4* v = reinterpret_cast<const float4*>(ring[c % kStrictStages]);
+      const uint64_t left = n - c * kStrictChunk;
+      const int cnt = left < (uint64_t)kStrictChunk ? (int)left : kStrictChunk;
+      int i = 0;
+#pragma unroll 8
+      for (; i + 4 <= cnt; i += 4) {
+        const float4 q = v[i / 4];
+        acc = __fadd_rn(acc, q.x);
+        acc = __fadd_rn(acc, q.y);
+        acc = __fadd_rn(acc, q.z);
+        acc = __fadd_rn(acc, q.w);
+      }
+      for (; i < cnt; ++i) acc = __fadd_rn(acc, ring[c % kStrictStages][i]);
+    }
+  }
+  cp_wait<0>();
+  if (threadIdx.x == 0) *out = acc;
+}
+
+}  // namespace
+
+int launch_fold_sum_strict(cudaStream_t s, const float* x, uint64_t n, float seed, float* out) {
+  if (aligned16(x))
+    fold_sum_strict_kernel<true><<<1, kStrictThreads, 0, s>>>(x, n, seed, out);
+  else
+    fold_sum_strict_kernel<false><<<1, kStrictThreads, 0, s>>>(x, n, seed, out);
+  count_launch();
+  return 0;
+}
+
 int launch_finalize_sum(cudaStream_t s, const double* total, float seed, float* out) {
   finalize_sum_kernel<<<1, 1, 0, s>>>(total, seed, out); count_launch();
   return 0;
@@ -124,5 +191,15 @@ extern "C" int mapal_gpu_fold_sum_f32(MapalGpuCtx* ctx, float seed, const float*
   DeviceSlot& d = ctx->dev[0];
   MAPAL_TRY(launch_fold_sum(d.stream, d.prof.sm_count, x, n, seed, d.fold_partials, d.fold_counter,
                             out, nullptr));
+  return finish(ctx, 0, false);
+}
+
+extern "C" int mapal_gpu_fold_sum_f32_strict(MapalGpuCtx* ctx, float seed, const float* x, uint64_t n,
+                                             float* out) {
+  MAPAL_TRY(enter(ctx));
+  if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
+  if (n && !x) return set_error(MAPAL_ERR_INVALID, "x is null");
+  DeviceSlot& d = ctx->dev[0];
+  MAPAL_TRY(launch_fold_sum_strict(d.stream, x, n, seed, out));
   return finish(ctx, 0, false);
 }

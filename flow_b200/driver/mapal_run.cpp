@@ -1,6 +1,6 @@
 // mapal_run.cpp — run a Mapal program's `main` with every bulk site on the GPU.
 //
-//   mapal-run [--device D] [--plan] program.mapal
+//   mapal-run [--device D] [--plan] [--fast-fold] program.mapal
 //
 // The reference compiles a program to CUDA C++ (`emit`, crates/backends/cuda/
 // src/lib.rs:72-111) and the emitted `main` launches one generated kernel per
@@ -22,7 +22,9 @@
 // through mapal_trap (exit 101); infrastructure errors exit 102 and programs
 // outside the subset are refused with exit 2 (EmitError::Unsupported).
 // --plan reads the program and prints the site calls it would make, without a
-// GPU (arrays are then shapes only).
+// GPU (arrays are then shapes only). Top-level f32 sum folds run in the
+// interpreter's order (bit-exact stdout); --fast-fold takes the bandwidth-bound
+// reordered tree instead, whose result is within its stated tolerance.
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -432,6 +434,7 @@ struct Value {
 
 struct Runner {
   bool plan = false;
+  bool fast_fold = false;  // the reordered f64 tree instead of the interpreter's order
   MapalGpuCtx* ctx = nullptr;
   std::map<std::string, Value> env;
 
@@ -719,11 +722,14 @@ struct Runner {
                    (b->kids[0]->s == L.params[1] && b->kids[1]->s == L.params[0]));
     if (!is_sum || xs.ty != TY_ARR || xs.elem != TY_F32 || seed.ty != TY_F32)
       unsupported("line %d: only the f32 sum fold runs at top level", line);
-    say("fold_sum_f32 n=" + std::to_string(xs.n));
+    say(std::string(fast_fold ? "fold_sum_f32" : "fold_sum_f32_strict") + " n=" + std::to_string(xs.n));
     if (plan) return num_f32(0);
     float* out = nullptr;
     if (cudaMalloc(&out, 4) != cudaSuccess) infra("cudaMalloc");
-    check(mapal_gpu_fold_sum_f32(ctx, seed.f, (const float*)xs.ptr(), xs.n, out), "fold_sum");
+    if (fast_fold)
+      check(mapal_gpu_fold_sum_f32(ctx, seed.f, (const float*)xs.ptr(), xs.n, out), "fold_sum");
+    else
+      check(mapal_gpu_fold_sum_f32_strict(ctx, seed.f, (const float*)xs.ptr(), xs.n, out), "fold_sum");
     sync_point();
     float r = 0;
     if (cudaMemcpy(&r, out, 4, cudaMemcpyDeviceToHost) != cudaSuccess) infra("cudaMemcpy");
@@ -1141,16 +1147,17 @@ struct Runner {
 }  // namespace
 
 int main(int argc, char** argv) {
-  bool plan = false;
+  bool plan = false, fast_fold = false;
   int device = 0;
   const char* path = nullptr;
   for (int a = 1; a < argc; ++a) {
     if (!strcmp(argv[a], "--plan")) plan = true;
+    else if (!strcmp(argv[a], "--fast-fold")) fast_fold = true;
     else if (!strcmp(argv[a], "--device") && a + 1 < argc) device = atoi(argv[++a]);
     else path = argv[a];
   }
   if (!path) {
-    fprintf(stderr, "usage: mapal-run [--device D] [--plan] program.mapal\n");
+    fprintf(stderr, "usage: mapal-run [--device D] [--plan] [--fast-fold] program.mapal\n");
     return 2;
   }
   FILE* f = fopen(path, "rb");
@@ -1168,6 +1175,7 @@ int main(int argc, char** argv) {
   std::vector<Chain> body = P.main_body();
   Runner R;
   R.plan = plan;
+  R.fast_fold = fast_fold;
   mapal_time_ms();  // start the process clock, as the reference's runtime does on first use
   if (!plan) {
     if (cudaSetDevice(device) != cudaSuccess) infra("cudaSetDevice");

@@ -320,6 +320,14 @@ int mapal_gpu_gather(MapalGpuCtx* ctx, const float* x, uint64_t n_x, const int32
  * within 1e-6 * sum|x| of the exact sum. */
 int mapal_gpu_fold_sum_f32(MapalGpuCtx* ctx, float seed, const float* x, uint64_t n, float* out);
 
+/* The sum fold in the interpreter's order: acc = seed; acc = acc + x[i] for
+ * i ascending, each add rounded to f32 (eval.rs:326-359), bit-exact with the
+ * interpreter and with the reference's one-thread fold kernel
+ * (kernel.rs:1484-1642). One block stages x through shared memory while one
+ * thread runs the dependent chain, so its time is n times the f32 add
+ * latency (about 2 ms per 2^20 elements), not a bandwidth bound. */
+int mapal_gpu_fold_sum_f32_strict(MapalGpuCtx* ctx, float seed, const float* x, uint64_t n, float* out);
+
 /* The same sum fold for callers that cannot allocate device memory: no
  * context, and no cudaMalloc / cudaFree or other allocation anywhere in the
  * call. This entry point has no counterpart in the reference.

@@ -96,7 +96,7 @@ def _driver_built():
     (P.conv2d(30), "tile_site rows=30 c=30 k=9 a{base=0 ci=0 ck=1 clane=0 ks=0/0/0} "
                    "b{base=0 ci=32 ck=0 clane=1 ks=3/32/1}"),
     (P.saxpy(1000), "saxpy n=1000"),
-    (P.reduce(1000), "fold_sum_f32 n=1000"),
+    (P.reduce(1000), "fold_sum_f32_strict n=1000"),
     (P.transpose(40), "move_site width=40 rows=40 cq=1 cr=40"),
     (P.gather(1000), "gather n=1000 n_x=1000"),
 ])

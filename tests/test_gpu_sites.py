@@ -232,6 +232,26 @@ def test_fold_sum_seed_and_specials(ctx):
     assert np.isnan(host(out)[0])
 
 
+@pytest.mark.parametrize("n", [0, 1, 3, 2047, 2048, 2049, 8195, 300007, (1 << 20) + 5])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_fold_sum_strict_bit_exact(ctx, n, offset):
+    # the interpreter's order, so fractional inputs give its exact last bits;
+    # offset 1 makes the input pointer 4-byte but not 16-byte aligned
+    x = o.gen(n + offset, 3, 0, fb.U11)
+    xd = dev(x)[offset:]
+    out = empty_f32(1)
+    ctx.fold_sum_strict(xd, out, seed=0.75)
+    assert same_bits(host(out), np.array([o.fold_sum(0.75, x[offset:])], np.float32))
+
+
+def test_fold_sum_strict_specials(ctx):
+    out = empty_f32(1)
+    ctx.fold_sum_strict(dev(np.array([1e30, -1e30, 1.0, np.float32(2.0**-30)], np.float32)), out)
+    assert host(out)[0] == np.float32(1.0) + np.float32(2.0**-30)
+    ctx.fold_sum_strict(dev(np.array([1.0, np.inf, -np.inf], np.float32)), out)
+    assert np.isnan(host(out)[0])
+
+
 # ---- FIR ---------------------------------------------------------------------------------------
 
 @pytest.mark.parametrize("n", [256, 65536, 1048576])

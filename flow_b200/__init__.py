@@ -79,12 +79,14 @@ def _check(rc: int) -> int:
 
 
 def _ptr(t) -> int:
-    """Device address of a buffer: a torch tensor, an int address, or None."""
+    """Address of a buffer: a torch tensor, a numpy array (host), an int address, or None."""
     if t is None:
         return 0
     if isinstance(t, int):
         return t
-    return t.data_ptr()
+    if hasattr(t, "data_ptr"):
+        return t.data_ptr()
+    return t.ctypes.data
 
 
 def _arr(ptrs: Sequence) -> ctypes.Array:
@@ -266,6 +268,11 @@ class Context:
 
     def matmul(self, site: TileSite, A, B, C, mode: int = STRICT) -> None:
         _check(lib().mapal_gpu_matmul_f32(self._h, ctypes.byref(site), _ptr(A), _ptr(B), _ptr(C), mode))
+
+    def matmul_host(self, site: TileSite, A, B, C, mode: int = STRICT) -> None:
+        """The matmul site on HOST buffers (torch CPU tensors, pinned for overlap, or
+        numpy arrays): copies in, multiply and copy out overlap in row blocks."""
+        _check(lib().mapal_gpu_matmul_f32_host(self._h, ctypes.byref(site), _ptr(A), _ptr(B), _ptr(C), mode))
 
     def tile_site(self, site: TileSite, a, b, out, mode: int = STRICT) -> None:
         _check(lib().mapal_gpu_tile_site_f32(self._h, ctypes.byref(site), _ptr(a), _ptr(b), _ptr(out), mode))

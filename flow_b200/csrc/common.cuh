@@ -56,6 +56,13 @@ struct DeviceSlot {
   // `stream` with events from `events` (created on first use, reused).
   cudaStream_t comm_stream = nullptr;
   std::vector<cudaEvent_t> events;
+  // Host-array entry points: copy streams (one per PCIe direction), their
+  // events and a growable device staging buffer, all created on first use.
+  cudaStream_t h2d_stream = nullptr;
+  cudaStream_t d2h_stream = nullptr;
+  std::vector<cudaEvent_t> host_events;
+  void* stage = nullptr;
+  size_t stage_bytes = 0;
   MapalGpuProfile prof{};
 };
 

@@ -170,6 +170,14 @@ static void free_slot(DeviceSlot& d) {
     cudaStreamDestroy(d.comm_stream);
   }
   for (cudaEvent_t e : d.events) cudaEventDestroy(e);
+  for (cudaStream_t s : {d.h2d_stream, d.d2h_stream}) {
+    if (s) {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  }
+  for (cudaEvent_t e : d.host_events) cudaEventDestroy(e);
+  cudaFree(d.stage);
   if (d.own_stream) cudaStreamDestroy(d.own_stream);
   d = DeviceSlot{};
 }

@@ -366,6 +366,19 @@ int mapal_gpu_conv2d_3x3_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const 
 int mapal_gpu_matmul_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* A,
                          const float* B, float* C, int mode);
 
+/* The same matmul site with A, B and C in HOST memory (the emitted program's
+ * host<->device seam, one call instead of a blocking cudaMemcpy per array).
+ * B is copied up first; A then goes up in row blocks on a copy stream while
+ * earlier blocks multiply, and each finished block of C comes back on a
+ * second copy stream, so with pinned (page-locked) host buffers the transfers
+ * in both directions overlap the arithmetic; pageable buffers work, with
+ * staged copies. Device memory is a staging buffer owned by the context
+ * (grown on demand, freed with it). Results equal mapal_gpu_matmul_f32's in
+ * the same mode. In async mode, C is complete once the context is
+ * synchronised; A, B and C must stay valid and unmodified until then. */
+int mapal_gpu_matmul_f32_host(MapalGpuCtx* ctx, const MapalTileSite* site, const float* A,
+                              const float* B, float* C, int mode);
+
 /* Any TileSite: dispatches to the matmul, FIR or conv2d kernel when the record
  * has that shape, else runs the generic one-thread-per-cell site kernel
  * (bit-exact, the rung-0 shape). mode applies to matmul-shaped sites. */

@@ -56,7 +56,7 @@ def test_strict_host_padded_and_offset(ctx):
     M, N, K = 600, 200, 50
     s = _site(M, N, K, lda=K + 3, ldb=N + 5, abase=7, bbase=2, seed=0.5)
     A, B = _inputs(s, seed=4)
-    rc, want = o.tile_site(s, A, B)
+    rc, want = o.tile_site(o.TileSite.from_buffer_copy(bytes(s)), A, B)  # same record layout
     assert rc == 0
     got = np.full(M * N, np.nan, np.float32)
     ctx.matmul_host(s, A, B, got)

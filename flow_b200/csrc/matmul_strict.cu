@@ -14,10 +14,12 @@
 //  * each thread owns TM x TN cells in registers and walks k in steps of 4:
 //    one 128-bit load brings 4 k-values of an A row, one brings 4 columns of
 //    a B row;
-//  * the products are scalar rounded multiplies and the adds of two
-//    neighbouring cells issue as one packed f32x2 add (3 issue slots per 2
-//    MACs instead of 4), leaving issue slots for the loads so the FP32 pipe,
-//    not issue, is the bound;
+//  * two neighbouring cells advance together: one packed FMA with a -0.0
+//    addend passed in at run time forms both rounded products, one packed
+//    add accumulates them (2 issue slots per 2 MACs; f32x2.cuh gives the
+//    argument that this is bit-identical to a rounded multiply then a
+//    rounded add), leaving issue slots for the loads so the FP32 pipe, not
+//    issue, is the bound;
 //  * no split-K: k is never partitioned, so no cell is reassociated.
 //
 // The roofline is the FP32 pipe at one operation per lane per clock
@@ -85,8 +87,9 @@ template <int BM, int BN, int BK, int TM, int TN, int STAGES, bool kVec>
 __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
     mm_strict_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
                      int M, int N, int K, long long lda, long long ldb, long long ldc, float seed,
-                     int tile_base, int tiles_n0, int acc_from_c) {
+                     int tile_base, int tiles_n0, int acc_from_c, float neg_zero) {
   using G = Cfg<BM, BN, BK, TM, TN, STAGES>;
+  const f2 z2 = f2_splat(neg_zero);  // -0.0, unknown to the compiler: see f2_mac_z
   extern __shared__ __align__(16) float smem[];
   float* As = smem;                              // [STAGES][BM][kAStride]
   float* Bs = smem + STAGES * G::kAStage;        // [STAGES][BK][kBStride]
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
           for (int i = 0; i < TM; ++i) {
             const float av = kk == 0 ? a[i].x : kk == 1 ? a[i].y : kk == 2 ? a[i].z : a[i].w;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac(acc[i][q], av, bv[2 * q], av, bv[2 * q + 1]);
+            for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac_z(acc[i][q], f2_splat(av), f2_pack(bv[2 * q], bv[2 * q + 1]), z2);
           }
         }
       }
@@ -199,7 +202,7 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
         for (int i = 0; i < TM; ++i) {
           const float av = as[a_row(i) * G::kAStride + kk];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac(acc[i][q], av, bv[2 * q], av, bv[2 * q + 1]);
+          for (int q = 0; q < 4; ++q) acc[i][q] = f2_mac_z(acc[i][q], f2_splat(av), f2_pack(bv[2 * q], bv[2 * q + 1]), z2);
         }
       }
     }
@@ -247,7 +250,7 @@ int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_
   const unsigned grid = (unsigned)ntiles * kSplit * kSplit;
   if (grid == 0) return 0;
   kern<<<grid, G::kThreads, G::kSmem, s>>>(A, B, C, (int)M, (int)N, (int)K, (long long)lda, (long long)ldb,
-                                           (long long)ldc, seed, tile_base, tiles_n0, acc_from_c); count_launch();
+                                           (long long)ldc, seed, tile_base, tiles_n0, acc_from_c, -0.0f); count_launch();
   return 0;
 }
 

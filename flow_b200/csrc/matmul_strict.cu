@@ -279,10 +279,10 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
   const int tiles112 = (int)((M + 127) / 128) * tiles_n112;
   const double t_narrow = ((tiles112 + sms - 1) / sms) * (112.0 / 128.0);
   if (t_narrow + 1e-9 < t_square)
-    return launch_cfg<128, 112, 32, 3, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, tiles112, tiles_n112,
+    return launch_cfg<128, 112, 64, 2, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, tiles112, tiles_n112,
                                              acc_from_c);
   const int full = split ? waves * sms : tiles;
-  MAPAL_TRY((launch_cfg<128, 128, 32, 3, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
+  MAPAL_TRY((launch_cfg<128, 128, 64, 2, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
                                                 acc_from_c)));
   return launch_cfg<64, 64, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, full, tiles - full,
                                          tiles_n0, acc_from_c);

@@ -562,7 +562,7 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
     if d.world == 1:
         # 2^20-class sites: back-to-back launches rotating
         # over enough buffer sets to exceed twice the L2, so no launch finds
-        # its inputs in L2 (flow_b200.sitebench).
+        # its inputs in L2, timed as a CUDA graph replay (flow_b200.sitebench).
         from flow_b200 import sitebench
         l2 = ctx.profile().l2_bytes
         sms = ctx.profile().sm_count
@@ -573,13 +573,15 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
                                    ("fir_2^20x64", "fir", 1 << 20, 64),
                                    ("conv2d_1024^2_3x3", "conv2d", 1024 * 1024, None)]:
             r = sitebench.measure(ctx, torch, site, size, k, reps=50, warmup=3, l2_bytes=l2)
-            extra = {"buffer_sets": r["buffer_sets"], "launches": r["launches"]}
+            extra = {"buffer_sets": r["buffer_sets"], "launches": r["launches"], "timing": r["timing"],
+                     "ms_host_issued": r["ms_host_issued"]}
             if site == "gather":
                 extra["bytes_basis"] = "algorithmic 12 B/element"
             if site == "fir":
                 extra["fp32_frac"] = r["gflops"] * 1e9 / (sms * 128 * pk["sm_max_mhz"] * 1e6)
             rec(key, r["bytes"], r["ms"], extra)
-        out["l2"] = ("2^20 class: launches rotate over buffer sets totalling > 2x L2; "
+        out["l2"] = ("2^20 class: launches rotate over buffer sets totalling > 2x L2 and are replayed "
+                     "from a CUDA graph (ms_host_issued: the same launches issued from Python); "
                      "2^30 class: inputs far larger than L2")
 
     # 2^30-class, sharded over the ranks (each rank its contiguous share).

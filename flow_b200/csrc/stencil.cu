@@ -11,8 +11,10 @@
 // seed, then acc + w[k]*x[...] for k ascending, each op rounded), so the
 // results are bit-identical to the interpreter's.
 //
-// Each thread computes two outputs half a tile apart as one packed pair: two
-// scalar rounded products and one packed rounded add (f32x2.cuh).
+// Each thread computes pairs of outputs half a tile apart as packed values
+// (f32x2.cuh): FIR forms both rounded products with one packed FMA whose
+// addend is a run-time -0.0; conv2d uses two scalar rounded products; both
+// accumulate with one packed rounded add.
 #include "common.cuh"
 #include "cpasync.cuh"
 #include "f32x2.cuh"
@@ -20,80 +22,88 @@
 namespace {
 
 // ---- FIR ---------------------------------------------------------------------
+//
+// A block computes kFirTile consecutive outputs as two lanes of kFirHalf: a
+// thread owns outputs j..j+3 of lane a and the same offsets of lane b, and
+// advances each (lane a, lane b) output pair as one packed value. The input
+// window is staged in shared memory interleaved, pair p = (x[t0 + p],
+// x[t0 + kFirHalf + p]), and every tap is staged as the splat pair (w, w), so
+// a 16-byte shared load yields two ready operand pairs and a MAC pair is one
+// packed FMA with a run-time -0.0 addend (the two rounded products) plus one
+// packed add (f32x2.cuh, f2_mac_z): no register moves in the loop.
 
-constexpr int kFirThreads = 64;
-constexpr int kFirR = 8;                       // outputs per thread per lane
+constexpr int kFirThreads = 128;
+constexpr int kFirR = 4;                       // outputs per thread per lane
 constexpr int kFirHalf = kFirThreads * kFirR;  // outputs per lane per block
 constexpr int kFirTile = 2 * kFirHalf;         // outputs per block
 
-__host__ __device__ constexpr int fir_wpad(int taps) { return (taps + 7) & ~7; }
+__host__ __device__ constexpr int fir_wpad(int taps) { return (taps + 3) & ~3; }
+// pairs staged per block: the last thread reads up to pair kFirHalf - kFirR + wpad + 3
+__host__ __device__ constexpr int fir_npairs(int taps) { return kFirHalf + fir_wpad(taps) + 4; }
 
 // y[t] = fold_k(acc + w[k] * x[t + k]) from seed, t in [0, n_out).
 __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restrict__ w, int taps,
                                                           const float* __restrict__ x, uint64_t x_len,
                                                           float* __restrict__ y, uint64_t n_out,
-                                                          float seed) {
+                                                          float seed, float neg_zero) {
   extern __shared__ __align__(16) float fir_smem[];
-  float* ws = fir_smem;                    // taps, zero-padded to a multiple of 8
-  float* xs = fir_smem + fir_wpad(taps);   // x[t0 .. t0 + tile + taps + 16)
-  const int span = (kFirTile + taps + 16 + 3) & ~3;  // staged floats, whole 16-byte groups
+  const int wpad = fir_wpad(taps), npairs = fir_npairs(taps);
+  float* wp = fir_smem;             // [wpad] splat pairs (w[k], w[k]), zero past the taps
+  float* xp = fir_smem + 2 * wpad;  // [npairs] pairs (x[t0 + p], x[t0 + kFirHalf + p])
   const uint64_t t0 = (uint64_t)blockIdx.x * kFirTile;
-  const bool xal = ((uintptr_t)x & 15) == 0, wal = ((uintptr_t)w & 15) == 0;
 
-  for (int c = threadIdx.x; c < fir_wpad(taps) / 4; c += kFirThreads) {
-    const int k = 4 * c;
-    copy4(smem_u32(ws + k), w + (k < taps ? k : 0), taps - k, wal);
+  for (int k = threadIdx.x; k < wpad; k += kFirThreads) {
+    const bool ok = k < taps;
+    cp_async4(smem_u32(wp + 2 * k), w + (ok ? k : 0), ok);
+    cp_async4(smem_u32(wp + 2 * k + 1), w + (ok ? k : 0), ok);
   }
-  for (int c = threadIdx.x; c < span / 4; c += kFirThreads) {
-    const uint64_t g = t0 + 4 * (uint64_t)c;
-    const int nvalid = g < x_len ? (int)(x_len - g < 4 ? x_len - g : 4) : 0;
-    copy4(smem_u32(xs + 4 * c), x + (nvalid > 0 ? g : 0), nvalid, xal);
+  for (int p = threadIdx.x; p < npairs; p += kFirThreads) {
+    const uint64_t ga = t0 + p, gb = t0 + kFirHalf + p;
+    cp_async4(smem_u32(xp + 2 * p), x + (ga < x_len ? ga : 0), ga < x_len);
+    cp_async4(smem_u32(xp + 2 * p + 1), x + (gb < x_len ? gb : 0), gb < x_len);
   }
   cp_commit();
   cp_wait<0>();
   __syncthreads();
 
-  const int ba = threadIdx.x * kFirR, bb = kFirHalf + threadIdx.x * kFirR;
+  const f2 z2 = f2_splat(neg_zero);  // -0.0, unknown to the compiler: see f2_mac_z
+  const ulonglong2* xv = reinterpret_cast<const ulonglong2*>(xp) + (kFirR / 2) * threadIdx.x;
+  const ulonglong2* wv = reinterpret_cast<const ulonglong2*>(wp);
   f2 acc[kFirR];
   const f2 s2 = f2_splat(seed);
 #pragma unroll
   for (int r = 0; r < kFirR; ++r) acc[r] = s2;
-  float ca[kFirR], cb[kFirR], na[kFirR], nb[kFirR];
-#pragma unroll
-  for (int r = 0; r < kFirR; r += 4) {
-    *reinterpret_cast<float4*>(ca + r) = *reinterpret_cast<const float4*>(xs + ba + r);
-    *reinterpret_cast<float4*>(cb + r) = *reinterpret_cast<const float4*>(xs + bb + r);
+  f2 win[2 * kFirR];  // pairs j + kg .. j + kg + 7
+  {
+    const ulonglong2 c0 = xv[0], c1 = xv[1];
+    win[0] = c0.x, win[1] = c0.y, win[2] = c1.x, win[3] = c1.y;
   }
-  for (int kg = 0; kg < taps; kg += kFirR) {
-    float w8[kFirR];
+  for (int kg = 0; kg < taps; kg += 4) {
+    const ulonglong2 n0 = xv[kg / 2 + 2], n1 = xv[kg / 2 + 3];
+    win[4] = n0.x, win[5] = n0.y, win[6] = n1.x, win[7] = n1.y;
+    const ulonglong2 w0 = wv[kg / 2], w1 = wv[kg / 2 + 1];
+    const f2 wk[4] = {w0.x, w0.y, w1.x, w1.y};
+    if (kg + 4 <= taps) {
 #pragma unroll
-    for (int r = 0; r < kFirR; r += 4) {
-      *reinterpret_cast<float4*>(na + r) = *reinterpret_cast<const float4*>(xs + ba + kg + kFirR + r);
-      *reinterpret_cast<float4*>(nb + r) = *reinterpret_cast<const float4*>(xs + bb + kg + kFirR + r);
-      *reinterpret_cast<float4*>(w8 + r) = *reinterpret_cast<const float4*>(ws + kg + r);
+      for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+        for (int r = 0; r < kFirR; ++r) acc[r] = f2_mac_z(acc[r], wk[kk], win[r + kk], z2);
+    } else {
+      // the last, partial tap group: exactly the remaining taps, in order
+#pragma unroll
+      for (int kk = 0; kk < 3; ++kk)
+        if (kk < taps - kg)
+#pragma unroll
+          for (int r = 0; r < kFirR; ++r) acc[r] = f2_mac_z(acc[r], wk[kk], win[r + kk], z2);
     }
 #pragma unroll
-    for (int kk = 0; kk < kFirR; ++kk) {
-      if (kg + kk < taps) {
-#pragma unroll
-        for (int r = 0; r < kFirR; ++r) {
-          const float xa = (r + kk < kFirR) ? ca[r + kk] : na[r + kk - kFirR];
-          const float xb = (r + kk < kFirR) ? cb[r + kk] : nb[r + kk - kFirR];
-          acc[r] = f2_mac(acc[r], w8[kk], xa, w8[kk], xb);
-        }
-      }
-    }
-#pragma unroll
-    for (int r = 0; r < kFirR; ++r) {
-      ca[r] = na[r];
-      cb[r] = nb[r];
-    }
+    for (int r = 0; r < 4; ++r) win[r] = win[r + 4];
   }
+  const uint64_t j = t0 + (uint64_t)kFirR * threadIdx.x;
 #pragma unroll
   for (int r = 0; r < kFirR; ++r) {
-    const uint64_t ta = t0 + ba + r, tb = t0 + bb + r;
-    if (ta < n_out) y[ta] = f2_lo(acc[r]);
-    if (tb < n_out) y[tb] = f2_hi(acc[r]);
+    if (j + r < n_out) y[j + r] = f2_lo(acc[r]);
+    if (j + kFirHalf + r < n_out) y[j + kFirHalf + r] = f2_hi(acc[r]);
   }
 }
 
@@ -172,7 +182,7 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
 // Shared-memory bytes of one FIR block, 0 if the taps do not fit.
 static size_t fir_smem_bytes(uint64_t taps) {
   if (taps > 8192) return 0;
-  return sizeof(float) * ((size_t)fir_wpad((int)taps) + (((size_t)kFirTile + (size_t)taps + 16 + 3) & ~(size_t)3));
+  return sizeof(float) * 2 * ((size_t)fir_wpad((int)taps) + (size_t)fir_npairs((int)taps));
 }
 
 int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, uint64_t x_len, float* y,
@@ -185,7 +195,8 @@ int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, ui
   }
   uint64_t blocks = (n_out + kFirTile - 1) / kFirTile;
   if (blocks > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
-  fir_kernel<<<(unsigned)blocks, kFirThreads, smem, s>>>(w, (int)taps, x, x_len, y, n_out, seed); count_launch();
+  fir_kernel<<<(unsigned)blocks, kFirThreads, smem, s>>>(w, (int)taps, x, x_len, y, n_out, seed, -0.0f);
+  count_launch();
   return 0;
 }
 

@@ -6,9 +6,11 @@
 Inputs are generated on the device from the seeded stream. Every launch
 reads data that is not in L2: the inputs are replicated into as many buffer
 sets as it takes to exceed twice the L2 size and the launches rotate through
-them, back to back, between two CUDA events (so launch latency overlaps the
-previous launch, as in a pipeline of sites). Sites whose inputs exceed the L2
-on their own use one set. Prints one JSON object per site.
+them, between two CUDA events. The launches are timed twice: issued one by
+one from Python (`ms_host_issued`; for sites of a few microseconds that is
+the host's call rate) and captured into a CUDA graph and replayed (`ms`: the
+GPU runs them back to back, as in a pipeline of sites). Sites whose inputs
+exceed the L2 on their own use one set. Prints one JSON object per site.
 """
 from __future__ import annotations
 
@@ -108,7 +110,8 @@ def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = f
 
 
 def measure(ctx, torch, name: str, n: int, k: int | None = None, reps: int = 20, warmup: int = 3,
-            mode: int = fb.STRICT, l2_bytes: int = 126 << 20, rotate: bool = True) -> dict:
+            mode: int = fb.STRICT, l2_bytes: int = 126 << 20, rotate: bool = True,
+            graph: bool = True) -> dict:
     mk, run, per, flops = make_site(ctx, torch, name, n, k, mode)
     nsets = max(1, math.ceil(2 * l2_bytes / per)) if rotate else 1
     sets = [mk(i) for i in range(nsets)]
@@ -119,15 +122,41 @@ def measure(ctx, torch, name: str, n: int, k: int | None = None, reps: int = 20,
     ctx.synchronize()
     total = max(reps, nsets)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # Host-issued: one library call per launch from Python. For sites of a few
+    # microseconds the GPU then waits on the host between launches.
     e0.record(stream)
     for i in range(total):
         run(sets[i % nsets])
     e1.record(stream)
     ctx.synchronize()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / total
+    ms_host = e0.elapsed_time(e1) / total
+    ms = ms_host
+    if graph:
+        # The same launches captured once into a CUDA graph and replayed: the
+        # GPU sees them back to back, as from a program that issues sites
+        # faster than they run.
+        cap = torch.cuda.Stream()
+        cap.wait_stream(stream)
+        ctx.set_stream(cap.cuda_stream)
+        g = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(total):
+                    run(sets[i % nsets])
+        finally:
+            ctx.set_stream(stream.cuda_stream)
+        g.replay()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / total
+        del g
     out = {"site": name, "n": n, "ms": ms, "bytes": per, "gbs": per / (ms * 1e-3) / 1e9,
-           "launches": total, "buffer_sets": nsets}
+           "launches": total, "buffer_sets": nsets, "ms_host_issued": ms_host,
+           "timing": "CUDA graph replay of the launches" if graph else "host-issued launches"}
     if flops:
         out["gflops"] = flops / (ms * 1e-3) / 1e9
     return out
@@ -142,6 +171,7 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--mode", choices=["strict", "tf32x3"], default="strict")
     ap.add_argument("--no-rotate", action="store_true")
+    ap.add_argument("--no-graph", action="store_true", help="time host-issued launches only")
     args = ap.parse_args()
     import torch
     defaults = {"saxpy": 1 << 20, "transpose": 1024 * 1024, "gather": 1 << 20, "sum": 1 << 20,
@@ -152,7 +182,8 @@ def main() -> int:
         mode = fb.TF32X3 if args.mode == "tf32x3" else fb.STRICT
         for s in sites:
             n = args.n or defaults[s]
-            r = measure(ctx, torch, s, n, args.k, args.reps, args.warmup, mode, l2, not args.no_rotate)
+            r = measure(ctx, torch, s, n, args.k, args.reps, args.warmup, mode, l2, not args.no_rotate,
+                        not args.no_graph)
             print(json.dumps(r), flush=True)
     return 0
 

@@ -7,15 +7,20 @@
 // and C in host memory makes one call: B goes up first (every row of C needs
 // all of it), then A streams up in row blocks on a copy stream while earlier
 // blocks multiply on the context stream, and each finished block of C streams
-// down on a second copy stream. With pinned host memory the two PCIe
-// directions and the SMs all run at once; the exposed cost is B's transfer,
-// the first A block and the last C block.
+// down on a second copy stream. In strict mode with K deep enough the upload
+// is cut along K instead: phase c brings up B's rows and A's columns of
+// k-range c while phase c-1 multiplies, and the last phase runs in row blocks
+// so C goes home block by block. With pinned host memory the two PCIe
+// directions and the SMs all run at once; the exposed cost is the first
+// phase's upload and the last C block.
 #include "common.cuh"
 
 namespace {
 
 constexpr uint64_t kBlockAlign = 128;  // rows: a whole number of strict-kernel tiles per block
 constexpr uint64_t kMaxBlocks = 8;
+constexpr uint64_t kPhases = 4;        // k-ranges of the strict pipeline
+constexpr uint64_t kPhaseMinK = 128;   // shallower ranges are not worth a launch each
 
 int host_streams(DeviceSlot& d, size_t nevents) {
   MAPAL_CUDA(cudaSetDevice(d.device));
@@ -75,7 +80,7 @@ extern "C" int mapal_gpu_matmul_f32_host(MapalGpuCtx* ctx, const MapalTileSite* 
     rows_per = (rows_per + kBlockAlign - 1) / kBlockAlign * kBlockAlign;
   }
   const uint64_t nblocks = (M + rows_per - 1) / rows_per;
-  MAPAL_TRY(host_streams(d, 2 * nblocks + 2));
+  MAPAL_TRY(host_streams(d, 2 * nblocks + kPhases + 2));
   MAPAL_TRY(stage_reserve(d, up256(a_elems * 4) + up256(b_elems * 4) + up256(c_elems * 4)));
   float* dA = (float*)d.stage;
   float* dB = (float*)((char*)d.stage + up256(a_elems * 4));
@@ -93,6 +98,40 @@ extern "C" int mapal_gpu_matmul_f32_host(MapalGpuCtx* ctx, const MapalTileSite* 
     MAPAL_CUDA(cudaEventRecord(ev[1], d.stream));
     MAPAL_CUDA(cudaStreamWaitEvent(d.d2h_stream, ev[1], 0));
     MAPAL_CUDA(cudaMemcpyAsync(C, dC, c_elems * 4, cudaMemcpyDeviceToHost, d.d2h_stream));
+  } else if (mode == MAPAL_MATMUL_STRICT && nblocks > 1 && K >= kPhases * kPhaseMinK) {
+    // K in phases: phase c brings up B's rows and A's columns of k-range c
+    // and multiplies them into C (each cell continues from the partial fold
+    // the previous phase left in C, the same f32 value, so the result is
+    // bit-identical to one pass). Only the first phase's transfer is exposed;
+    // the last phase runs in row blocks whose C blocks go home as they finish.
+    const uint64_t kc_len = ((K + kPhases - 1) / kPhases + 63) / 64 * 64;
+    const uint64_t nph = (K + kc_len - 1) / kc_len;
+    for (uint64_t c = 0; c < nph; ++c) {
+      const uint64_t k0 = c * kc_len, kc = k0 + kc_len < K ? kc_len : K - k0;
+      const uint64_t b_lo = k0 * ldb, b_hi = (k0 + kc - 1) * ldb + N;
+      MAPAL_CUDA(cudaMemcpyAsync(dB + b_lo, B + site->b.base + b_lo, (b_hi - b_lo) * 4, cudaMemcpyHostToDevice,
+                                 d.h2d_stream));
+      MAPAL_CUDA(cudaMemcpy2DAsync(dA + k0, lda * 4, A + site->a.base + k0, lda * 4, kc * 4, M,
+                                   cudaMemcpyHostToDevice, d.h2d_stream));
+      MAPAL_CUDA(cudaEventRecord(ev[2 + c], d.h2d_stream));
+      MAPAL_CUDA(cudaStreamWaitEvent(d.stream, ev[2 + c], 0));
+      if (c + 1 < nph) {
+        MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, dA + k0, dB + b_lo, dC, M, N, kc, lda, ldb, N,
+                                          site->seed, c > 0));
+        continue;
+      }
+      for (uint64_t blk = 0; blk < nblocks; ++blk) {
+        const uint64_t r0 = blk * rows_per;
+        const uint64_t r1 = r0 + rows_per < M ? r0 + rows_per : M;
+        cudaEvent_t done = ev[2 + nph + blk];
+        MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, dA + r0 * lda + k0, dB + b_lo, dC + r0 * N,
+                                          r1 - r0, N, kc, lda, ldb, N, site->seed, c > 0));
+        MAPAL_CUDA(cudaEventRecord(done, d.stream));
+        MAPAL_CUDA(cudaStreamWaitEvent(d.d2h_stream, done, 0));
+        MAPAL_CUDA(cudaMemcpyAsync(C + r0 * N, dC + r0 * N, (r1 - r0) * N * 4, cudaMemcpyDeviceToHost,
+                                   d.d2h_stream));
+      }
+    }
   } else {
     MAPAL_CUDA(cudaMemcpyAsync(dB, B + site->b.base, b_elems * 4, cudaMemcpyHostToDevice, d.h2d_stream));
     for (uint64_t blk = 0; blk < nblocks; ++blk) {

@@ -34,7 +34,9 @@ def _inputs(s, seed=11):
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 1, 1), (77, 130, 33), (300, 257, 64), (1000, 260, 77),
-                                   (1024, 1024, 256), (2049, 96, 40)])
+                                   (1024, 1024, 256), (2049, 96, 40),
+                                   # deep K: the strict path uploads and multiplies in k-range phases
+                                   (777, 300, 600), (1030, 513, 1000), (520, 64, 4096)])
 @pytest.mark.parametrize("pinned", [True, False])
 def test_strict_host_bit_exact(ctx, M, N, K, pinned):
     s = _site(M, N, K)
@@ -52,8 +54,9 @@ def test_strict_host_bit_exact(ctx, M, N, K, pinned):
     assert same_bits(got, want), first_diff(got, want)
 
 
-def test_strict_host_padded_and_offset(ctx):
-    M, N, K = 600, 200, 50
+@pytest.mark.parametrize("K", [50, 700])
+def test_strict_host_padded_and_offset(ctx, K):
+    M, N = 600, 200
     s = _site(M, N, K, lda=K + 3, ldb=N + 5, abase=7, bbase=2, seed=0.5)
     A, B = _inputs(s, seed=4)
     rc, want = o.tile_site(o.TileSite.from_buffer_copy(bytes(s)), A, B)  # same record layout

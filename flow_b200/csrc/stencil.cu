@@ -30,7 +30,10 @@ namespace {
 // x[t0 + kFirHalf + p]), and every tap is staged as the splat pair (w, w), so
 // a 16-byte shared load yields two ready operand pairs and a MAC pair is one
 // packed FMA with a run-time -0.0 addend (the two rounded products) plus one
-// packed add (f32x2.cuh, f2_mac_z): no register moves in the loop.
+// packed add (f32x2.cuh, f2_mac_z). The loads of the next tap group are issued
+// a group ahead, and the 16-byte units are split into even and odd arrays so
+// the units a warp reads in one instruction are consecutive (no bank
+// conflicts).
 
 constexpr int kFirThreads = 128;
 constexpr int kFirR = 4;                       // outputs per thread per lane
@@ -38,8 +41,9 @@ constexpr int kFirHalf = kFirThreads * kFirR;  // outputs per lane per block
 constexpr int kFirTile = 2 * kFirHalf;         // outputs per block
 
 __host__ __device__ constexpr int fir_wpad(int taps) { return (taps + 3) & ~3; }
-// pairs staged per block: the last thread reads up to pair kFirHalf - kFirR + wpad + 3
-__host__ __device__ constexpr int fir_npairs(int taps) { return kFirHalf + fir_wpad(taps) + 4; }
+// pairs staged per block (a multiple of 4): the last thread's prefetch reads up
+// to pair 4*(kFirThreads-1) + wpad + 7
+__host__ __device__ constexpr int fir_npairs(int taps) { return kFirHalf + fir_wpad(taps) + 8; }
 
 // y[t] = fold_k(acc + w[k] * x[t + k]) from seed, t in [0, n_out).
 __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restrict__ w, int taps,
@@ -48,41 +52,49 @@ __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restric
                                                           float seed, float neg_zero) {
   extern __shared__ __align__(16) float fir_smem[];
   const int wpad = fir_wpad(taps), npairs = fir_npairs(taps);
-  float* wp = fir_smem;             // [wpad] splat pairs (w[k], w[k]), zero past the taps
-  float* xp = fir_smem + 2 * wpad;  // [npairs] pairs (x[t0 + p], x[t0 + kFirHalf + p])
+  float* wp = fir_smem;                   // [wpad + 4] splat pairs (w[k], w[k]), zero past the taps
+  float* xe = fir_smem + 2 * (wpad + 4);  // even 16-byte units of the pair array
+  float* xo = xe + npairs;                // odd units
   const uint64_t t0 = (uint64_t)blockIdx.x * kFirTile;
 
-  for (int k = threadIdx.x; k < wpad; k += kFirThreads) {
+  for (int k = threadIdx.x; k < wpad + 4; k += kFirThreads) {
     const bool ok = k < taps;
     cp_async4(smem_u32(wp + 2 * k), w + (ok ? k : 0), ok);
     cp_async4(smem_u32(wp + 2 * k + 1), w + (ok ? k : 0), ok);
   }
+  // pair p = (x[t0 + p], x[t0 + kFirHalf + p]) lives in unit u = p/2 (two
+  // pairs per 16 bytes); even units go to xe, odd ones to xo, so the units a
+  // warp reads in one instruction are consecutive.
   for (int p = threadIdx.x; p < npairs; p += kFirThreads) {
     const uint64_t ga = t0 + p, gb = t0 + kFirHalf + p;
-    cp_async4(smem_u32(xp + 2 * p), x + (ga < x_len ? ga : 0), ga < x_len);
-    cp_async4(smem_u32(xp + 2 * p + 1), x + (gb < x_len ? gb : 0), gb < x_len);
+    const int u = p >> 1;
+    float* dst = ((u & 1) ? xo : xe) + 4 * (u >> 1) + 2 * (p & 1);
+    cp_async4(smem_u32(dst), x + (ga < x_len ? ga : 0), ga < x_len);
+    cp_async4(smem_u32(dst + 1), x + (gb < x_len ? gb : 0), gb < x_len);
   }
   cp_commit();
   cp_wait<0>();
   __syncthreads();
 
   const f2 z2 = f2_splat(neg_zero);  // -0.0, unknown to the compiler: see f2_mac_z
-  const ulonglong2* xv = reinterpret_cast<const ulonglong2*>(xp) + (kFirR / 2) * threadIdx.x;
+  const ulonglong2* ev = reinterpret_cast<const ulonglong2*>(xe) + threadIdx.x;
+  const ulonglong2* ov = reinterpret_cast<const ulonglong2*>(xo) + threadIdx.x;
   const ulonglong2* wv = reinterpret_cast<const ulonglong2*>(wp);
   f2 acc[kFirR];
   const f2 s2 = f2_splat(seed);
 #pragma unroll
   for (int r = 0; r < kFirR; ++r) acc[r] = s2;
-  f2 win[2 * kFirR];  // pairs j + kg .. j + kg + 7
+  f2 win[8];  // pairs 4*tid + kg .. 4*tid + kg + 7
   {
-    const ulonglong2 c0 = xv[0], c1 = xv[1];
+    const ulonglong2 c0 = ev[0], c1 = ov[0];
     win[0] = c0.x, win[1] = c0.y, win[2] = c1.x, win[3] = c1.y;
   }
+  // loads for the next tap group are issued one group ahead
+  ulonglong2 pe = ev[1], po = ov[1], pw0 = wv[0], pw1 = wv[1];
   for (int kg = 0; kg < taps; kg += 4) {
-    const ulonglong2 n0 = xv[kg / 2 + 2], n1 = xv[kg / 2 + 3];
-    win[4] = n0.x, win[5] = n0.y, win[6] = n1.x, win[7] = n1.y;
-    const ulonglong2 w0 = wv[kg / 2], w1 = wv[kg / 2 + 1];
-    const f2 wk[4] = {w0.x, w0.y, w1.x, w1.y};
+    win[4] = pe.x, win[5] = pe.y, win[6] = po.x, win[7] = po.y;
+    const f2 wk[4] = {pw0.x, pw0.y, pw1.x, pw1.y};
+    pe = ev[kg / 4 + 2], po = ov[kg / 4 + 2], pw0 = wv[kg / 2 + 2], pw1 = wv[kg / 2 + 3];
     if (kg + 4 <= taps) {
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
@@ -182,7 +194,7 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
 // Shared-memory bytes of one FIR block, 0 if the taps do not fit.
 static size_t fir_smem_bytes(uint64_t taps) {
   if (taps > 8192) return 0;
-  return sizeof(float) * 2 * ((size_t)fir_wpad((int)taps) + (size_t)fir_npairs((int)taps));
+  return sizeof(float) * 2 * ((size_t)fir_wpad((int)taps) + 4 + (size_t)fir_npairs((int)taps));
 }
 
 int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, uint64_t x_len, float* y,

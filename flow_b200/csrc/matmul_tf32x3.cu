@@ -152,17 +152,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Tile numbering: groups of kGroupRows tile rows, column-major inside a group,
+// so the CTAs of one wave share a few row panels of A and a band of B's
+// columns instead of every column of B (fewer L2 misses at large N and K).
+constexpr int kGroupRows = 8;
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int per_group = kGroupRows * tiles_n;
+  const int g = tile / per_group, r = tile % per_group;
+  const int rows = tiles_m - g * kGroupRows < kGroupRows ? tiles_m - g * kGroupRows : kGroupRows;
+  tm = g * kGroupRows + r % rows;
+  tn = r / rows;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     mm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                      const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                      float* __restrict__ C, int M, int N, int K, long long ldc, float seed, unsigned* flag,
-                     int tiles_n, int tile_base, int nsplit, float* __restrict__ part_out) {
+                     int tiles_m, int tiles_n, int tile_base, int nsplit, float* __restrict__ part_out) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  // CTA -> (tile, k part): tiles are numbered row-major over tiles_n columns.
+  // CTA -> (tile, k part); tile -> (tile row, tile column) by tile_coords.
   const int tile = tile_base + (int)blockIdx.x / nsplit, part = (int)blockIdx.x % nsplit;
-  const int m0 = (tile / tiles_n) * BM, n0 = (tile % tiles_n) * BN;
+  int tm, tn;
+  tile_coords(tile, tiles_m, tiles_n, tm, tn);
+  const int m0 = tm * BM, n0 = tn * BN;
   const int KT = (K + BK - 1) / BK;
   const int kt_lo = (int)((long long)KT * part / nsplit), nkt = (int)((long long)KT * (part + 1) / nsplit) - kt_lo;
 
@@ -292,14 +306,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 // tiles part[(r * nsplit + p)], for the k-split remainder tiles. Fixed order,
 // so the result is the same on every run.
 __global__ void reduce_parts_kernel(const float* __restrict__ part, float* __restrict__ C, int M, int N,
-                                    long long ldc, float seed, int tiles_n, int tile_base, int ntiles, int nsplit) {
+                                    long long ldc, float seed, int tiles_m, int tiles_n, int tile_base, int ntiles,
+                                    int nsplit) {
   const long long total = (long long)ntiles * BM * BN;
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
        e += (long long)gridDim.x * blockDim.x) {
     const int r = (int)(e / (BM * BN)), within = (int)(e % (BM * BN));
     const int row = within / BN, col = within % BN;
-    const int tile = tile_base + r;
-    const int m = (tile / tiles_n) * BM + row, n = (tile % tiles_n) * BN + col;
+    int tm, tn;
+    tile_coords(tile_base + r, tiles_m, tiles_n, tm, tn);
+    const int m = tm * BM + row, n = tn * BN + col;
     if (m >= M || n >= N) continue;
     float acc = 0.0f;
     for (int p = 0; p < nsplit; ++p) acc += part[((long long)r * nsplit + p) * (BM * BN) + within];
@@ -422,7 +438,8 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   // tiles a reduction kernel sums in a fixed order.
   const int sms = d.prof.sm_count;
   const int tiles_n = (int)((N + BN - 1) / BN);
-  const int tiles = (int)((M + BM - 1) / BM) * tiles_n;
+  const int tiles_m = (int)((M + BM - 1) / BM);
+  const int tiles = tiles_m * tiles_n;
   const int KT = (int)((K + BK - 1) / BK);
   const int full = (tiles / sms) * sms, rem = tiles - full;
   int nsplit = 1;
@@ -461,19 +478,19 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   const int whole = nsplit > 1 ? full : tiles;  // tiles computed over all of K
   if (whole > 0) {
     mm_tf32x3_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N,
-                                                                    (int)K, (long long)ldc, seed, d.trap, tiles_n, 0,
-                                                                    1, nullptr);
+                                                                    (int)K, (long long)ldc, seed, d.trap, tiles_m,
+                                                                    tiles_n, 0, 1, nullptr);
     count_launch();
   }
   if (nsplit > 1) {
     mm_tf32x3_kernel<<<(unsigned)(rem * nsplit), kThreads, smem, d.stream>>>(
-        m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_n, full, nsplit,
-        parts);
+        m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, full,
+        nsplit, parts);
     count_launch();
     const uint64_t n_red = (uint64_t)rem * BM * BN;
     reduce_parts_kernel<<<stream_grid(n_red, 256, sms, 8), 256, 0, d.stream>>>(parts, C, (int)M, (int)N,
-                                                                              (long long)ldc, seed, tiles_n, full,
-                                                                              rem, nsplit);
+                                                                              (long long)ldc, seed, tiles_m, tiles_n,
+                                                                              full, rem, nsplit);
     count_launch();
   }
   return 0;

@@ -77,17 +77,22 @@ struct Cfg {
 };
 
 // Work is laid out on a grid of parent tiles of 128 rows and BN*split
-// columns (tiles_n0 per row of tiles), split = 128/BM. A CTA covers one
+// columns (tiles_m x tiles_n0 of them), split = 128/BM. A CTA covers one
 // split^2-th of a parent tile: CTA u takes sub-tile u % split^2 of parent
-// tile tile_base + u / split^2.
+// tile tile_base + u / split^2. Parent tiles are numbered in groups of
+// kGroupRows tile rows, column-major inside a group, so the CTAs of one wave
+// share a few row panels of A and a band of B's columns (at N = 16384 a
+// row-major wave would stream all of B through L2 once per wave).
 // With acc_from_c the cells start from the values already in C (a partial
 // fold carried over from an earlier k range, bit-exact because the carried
 // accumulator is the same f32 value) instead of from the seed.
+constexpr int kGroupRows = 8;
+
 template <int BM, int BN, int BK, int TM, int TN, int STAGES, bool kVec>
 __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
     mm_strict_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C,
                      int M, int N, int K, long long lda, long long ldb, long long ldc, float seed,
-                     int tile_base, int tiles_n0, int acc_from_c, float neg_zero) {
+                     int tile_base, int tiles_m, int tiles_n0, int acc_from_c, float neg_zero) {
   using G = Cfg<BM, BN, BK, TM, TN, STAGES>;
   const f2 z2 = f2_splat(neg_zero);  // -0.0, unknown to the compiler: see f2_mac_z
   extern __shared__ __align__(16) float smem[];
@@ -100,8 +105,12 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
   static_assert(128 % BM == 0, "CTA rows divide the 128-row parent tile");
   const int parent = tile_base + (int)blockIdx.x / (kSplit * kSplit);
   const int sub = (int)blockIdx.x % (kSplit * kSplit);
-  const int m0 = (parent / tiles_n0) * (BM * kSplit) + (sub / kSplit) * BM;
-  const int n0 = (parent % tiles_n0) * (BN * kSplit) + (sub % kSplit) * BN;
+  const int per_group = kGroupRows * tiles_n0;
+  const int grp = parent / per_group, in_grp = parent % per_group;
+  const int grp_rows = tiles_m - grp * kGroupRows < kGroupRows ? tiles_m - grp * kGroupRows : kGroupRows;
+  const int pm = grp * kGroupRows + in_grp % grp_rows, pn = in_grp / grp_rows;
+  const int m0 = pm * (BM * kSplit) + (sub / kSplit) * BM;
+  const int n0 = pn * (BN * kSplit) + (sub % kSplit) * BN;
   const int KT = (K + BK - 1) / BK;
 
   // Loader coordinates: A tile BM x BK in 16-byte groups, B tile BK x BN.
@@ -250,7 +259,9 @@ int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_
   const unsigned grid = (unsigned)ntiles * kSplit * kSplit;
   if (grid == 0) return 0;
   kern<<<grid, G::kThreads, G::kSmem, s>>>(A, B, C, (int)M, (int)N, (int)K, (long long)lda, (long long)ldb,
-                                           (long long)ldc, seed, tile_base, tiles_n0, acc_from_c, -0.0f); count_launch();
+                                           (long long)ldc, seed, tile_base, (int)((M + 127) / 128), tiles_n0,
+                                           acc_from_c, -0.0f);
+  count_launch();
   return 0;
 }
 

@@ -280,18 +280,9 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
   // longer than the partial wave.
   const int waves = tiles / sms, rem = tiles - waves * sms;
   const bool split = rem > 0 && (4 * rem + sms - 1) / sms <= 2;
-  // Estimated time in 128 x 128 wave units.
-  const double t_square = waves + (rem == 0 ? 0.0 : split ? 0.65 : 1.0);
-  // Alternative: 128 x 112 tiles in whole waves. A row of 37 of them spans
-  // 4144 columns, so at N = 4096 four row bands are exactly 148 tiles: the
-  // row-block sizes 512..2048 of the sharded site fill every SM. A CTA does
-  // 112/128 of a square tile's work at the same per-SM rate.
-  const int tiles_n112 = (int)((N + 111) / 112);
-  const int tiles112 = (int)((M + 127) / 128) * tiles_n112;
-  const double t_narrow = ((tiles112 + sms - 1) / sms) * (112.0 / 128.0);
-  if (t_narrow + 1e-9 < t_square)
-    return launch_cfg<128, 112, 64, 2, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, tiles112, tiles_n112,
-                                             acc_from_c);
+  // (128 x 112 tiles, 37 per 4144 columns so that four row bands fill 148
+  // SMs, were measured too: with this kernel a wave of them takes as long as
+  // a wave of 128 x 128 tiles, so they never beat the plan above.)
   const int full = split ? waves * sms : tiles;
   MAPAL_TRY((launch_cfg<128, 128, 64, 2, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
                                                 acc_from_c)));

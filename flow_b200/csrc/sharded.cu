@@ -36,13 +36,15 @@ int check_arrays(MapalGpuCtx* ctx, const void* a, const void* b, const void* c) 
   return 0;
 }
 
-// Strict row-block matmul with the B broadcast overlapped: K is cut into
-// kChunks ranges; the broadcast of B's rows for range c runs on the comm
-// stream while range c-1 is multiplied on the compute stream. Range c > 0
-// continues every cell from the partial fold range c-1 left in C, so each
-// cell still folds k = 0..K-1 in order from the seed: bit-identical to one
-// pass.
-constexpr int kChunks = 4;
+// Strict row-block matmul with the B broadcast overlapped: K is cut into up
+// to kChunks ranges, [0, K/8), [K/8, 3K/8), [3K/8, K) (cuts rounded up to
+// whole 64-deep k-tiles); the broadcast of B's rows for range c runs on the
+// comm stream while range c-1 is multiplied on the compute stream, so only
+// the first eighth of B's transfer is exposed and each range's multiply is
+// longer than the next range's transfer. Range c > 0 continues every cell
+// from the partial fold range c-1 left in C, so each cell still folds
+// k = 0..K-1 in order from the seed: bit-identical to one pass.
+constexpr int kChunks = 3;
 
 int matmul_sharded_overlapped(MapalGpuCtx* ctx, const MapalTileSite* site, const float* const* A,
                               float* const* B, float* const* C, const uint64_t* m, int root) {
@@ -68,19 +70,28 @@ int matmul_sharded_overlapped(MapalGpuCtx* ctx, const MapalTileSite* site, const
     MAPAL_CUDA(cudaStreamWaitEvent(d.comm_stream, d.events[kChunks], 0));
   }
   uint64_t k_lo[kChunks + 1];
-  for (int c = 0; c <= kChunks; ++c) k_lo[c] = K * (uint64_t)c / kChunks;
-  for (int c = 0; c < kChunks; ++c) {
+  int nchunks = 0;
+  {
+    const uint64_t eighths[kChunks] = {0, 1, 3};
+    k_lo[0] = 0;
+    for (int c = 1; c < kChunks; ++c) {
+      uint64_t cut = (K * eighths[c] / 8 + 63) / 64 * 64;
+      if (cut > k_lo[nchunks] && cut < K) k_lo[++nchunks] = cut;
+    }
+    k_lo[++nchunks] = K;
+  }
+  for (int c = 0; c < nchunks; ++c) {
     // B rows [k_lo[c], k_lo[c+1]) within the B record's extent.
     const uint64_t lo = site->b.base + k_lo[c] * ldb;
     uint64_t hi = site->b.base + k_lo[c + 1] * ldb;
-    if (c == kChunks - 1 || hi > site->b.len) hi = site->b.len;
+    if (c == nchunks - 1 || hi > site->b.len) hi = site->b.len;
     MAPAL_TRY(nccl_broadcast_f32_on(ctx, B, lo, hi - lo, root, true));
     for (int i = 0; i < nd; ++i) {
       MAPAL_TRY(enter(ctx, i));
       MAPAL_CUDA(cudaEventRecord(ctx->dev[i].events[c], ctx->dev[i].comm_stream));
     }
   }
-  for (int c = 0; c < kChunks; ++c) {
+  for (int c = 0; c < nchunks; ++c) {
     for (int i = 0; i < nd; ++i) {
       DeviceSlot& d = ctx->dev[i];
       MAPAL_TRY(enter(ctx, i));

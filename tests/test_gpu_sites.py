@@ -325,7 +325,7 @@ def test_matmul_known_answers(ctx, case):
 
 @pytest.mark.parametrize("M,N,K", [(5, 20, 7), (6, 32, 5), (33, 65, 70), (128, 128, 128), (1, 1, 1),
                                    (257, 129, 1000), (1024, 1024, 1024), (300, 4097, 19), (127, 128, 129),
-                                   # 128x112 tiling (row blocks of the sharded 4096^2 site)
+                                   # row blocks of the sharded 4096^2 site (whole waves + 64x64 remainder)
                                    (512, 4096, 64), (2048, 4096, 40), (1000, 4000, 33)])
 def test_matmul_random(ctx, M, N, K):
     A = o.gen(M * K, 0, 0)

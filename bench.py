@@ -40,7 +40,7 @@ N_MM = 4096
 SEED_MM = 2
 # The reference's published number for this metric: its rung-0 CUDA kernel,
 # N=4096 f32, FMA off (bit-exact face), 57.2 ms on an RTX 4090.
-BASELINE_TFLOPS = 2.40
+PUBLISHED_REF_TFLOPS = 2.40
 HBM_FALLBACK_GBS = 6650.0
 
 
@@ -474,7 +474,7 @@ def run_ours(args) -> int:
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": d.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": value / BASELINE_TFLOPS,
+        "vs_baseline": value / PUBLISHED_REF_TFLOPS,
         "vs_baseline_ref": "reference rung-0 CUDA matmul N=4096 f32, 57.2 ms = 2.40 TFLOP/s on RTX 4090 "
                            "(docs/performance/matmul/s23.md:18)",
         "dtype": "f32", "data": "synthetic: A, B uniform[-1,1) from seed 2 (seeded i32-hash stream), on device",
@@ -496,7 +496,7 @@ def run_ours(args) -> int:
 
 
 def run_matmul_16384(ctx, d, fb, torch, pk) -> dict:
-    """The 16384^2 row-sharded matmul: A, B uniform[-1,1)
+    """The 16384^2 row-sharded matmul (the row-sharded 16384^2 workload): A, B uniform[-1,1)
     from seed 4, A row blocks per rank, B broadcast from rank 0 inside every
     step; strict and 3xTF32, 1 warm-up + 2 timed steps each (inputs are 1 GiB
     each, far beyond L2)."""
@@ -560,7 +560,7 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
         out[name] = r
 
     if d.world == 1:
-        # 2^20-class sites: back-to-back launches rotating
+        # 2^20-class sites (the streaming shapes at 2^20 elements): back-to-back launches rotating
         # over enough buffer sets to exceed twice the L2, so no launch finds
         # its inputs in L2, timed as a CUDA graph replay (flow_b200.sitebench).
         from flow_b200 import sitebench

@@ -19,7 +19,7 @@ namespace {
 
 constexpr uint64_t kBlockAlign = 128;  // rows: a whole number of strict-kernel tiles per block
 constexpr uint64_t kMaxBlocks = 8;
-constexpr uint64_t kPhases = 4;        // k-ranges of the strict pipeline
+constexpr uint64_t kPhases = 5;        // k-ranges of the strict pipeline (at most)
 constexpr uint64_t kPhaseMinK = 128;   // shallower ranges are not worth a launch each
 
 int host_streams(DeviceSlot& d, size_t nevents) {
@@ -98,16 +98,27 @@ extern "C" int mapal_gpu_matmul_f32_host(MapalGpuCtx* ctx, const MapalTileSite* 
     MAPAL_CUDA(cudaEventRecord(ev[1], d.stream));
     MAPAL_CUDA(cudaStreamWaitEvent(d.d2h_stream, ev[1], 0));
     MAPAL_CUDA(cudaMemcpyAsync(C, dC, c_elems * 4, cudaMemcpyDeviceToHost, d.d2h_stream));
-  } else if (mode == MAPAL_MATMUL_STRICT && nblocks > 1 && K >= kPhases * kPhaseMinK) {
+  } else if (mode == MAPAL_MATMUL_STRICT && nblocks > 1 && K >= 4 * kPhaseMinK) {
     // K in phases: phase c brings up B's rows and A's columns of k-range c
     // and multiplies them into C (each cell continues from the partial fold
     // the previous phase left in C, the same f32 value, so the result is
     // bit-identical to one pass). Only the first phase's transfer is exposed;
     // the last phase runs in row blocks whose C blocks go home as they finish.
-    const uint64_t kc_len = ((K + kPhases - 1) / kPhases + 63) / 64 * 64;
-    const uint64_t nph = (K + kc_len - 1) / kc_len;
+    // Cuts at 1/16, 3/16, 6/16 and 10/16 of K (whole 64-deep k-tiles): the
+    // first upload is small, each later one arrives before the multiply
+    // reaches it (a k-step uploads in ~0.6 us at 55 GB/s and multiplies in
+    // ~1 us at N = 4096), and the last phase is long enough to hide the
+    // download of C behind its row blocks.
+    uint64_t cut[kPhases + 2];
+    uint64_t nph = 0;
+    cut[0] = 0;
+    for (uint64_t sixteenths : {1, 3, 6, 10}) {
+      const uint64_t c = (K * sixteenths / 16 + 63) / 64 * 64;
+      if (c > cut[nph] && c < K) cut[++nph] = c;
+    }
+    cut[++nph] = K;
     for (uint64_t c = 0; c < nph; ++c) {
-      const uint64_t k0 = c * kc_len, kc = k0 + kc_len < K ? kc_len : K - k0;
+      const uint64_t k0 = cut[c], kc = cut[c + 1] - cut[c];
       const uint64_t b_lo = k0 * ldb, b_hi = (k0 + kc - 1) * ldb + N;
       MAPAL_CUDA(cudaMemcpyAsync(dB + b_lo, B + site->b.base + b_lo, (b_hi - b_lo) * 4, cudaMemcpyHostToDevice,
                                  d.h2d_stream));

@@ -365,28 +365,36 @@ __global__ void split_rows_kernel(const float* __restrict__ A, long long lda, in
   }
 }
 
-// B (K x N, row stride ldb) -> hiT, loT (N x K, row stride kp): 32x32 tiles
-// through shared memory so both sides stay coalesced.
-__global__ void split_transpose_kernel(const float* __restrict__ B, long long ldb, int K, int N,
-                                       float* __restrict__ hiT, float* __restrict__ loT, long long kp) {
-  __shared__ float th[32][33], tl[32][33];
-  const int k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+// B (K x N, row stride ldb) -> hiT, loT (N x K, row stride kp): 64x64 tiles
+// through shared memory so both sides stay coalesced; 256 threads, 16
+// elements each, all 16 loads in flight before the first shared store.
+constexpr int kTT = 64, kTRows = 4;
+__global__ void __launch_bounds__(kTT* kTRows) split_transpose_kernel(const float* __restrict__ B, long long ldb,
+                                                                     int K, int N, float* __restrict__ hiT,
+                                                                     float* __restrict__ loT, long long kp) {
+  __shared__ float th[kTT][kTT + 1], tl[kTT][kTT + 1];
+  const int k0 = blockIdx.y * kTT, n0 = blockIdx.x * kTT;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 64 x 4
+  float v[kTT / kTRows];
 #pragma unroll
-  for (int p = 0; p < 32; p += 8) {
-    const int k = k0 + ty + p, n = n0 + tx;
-    float h = 0.f, l = 0.f;
-    if (k < K && n < N) split1(__ldg(B + (long long)k * ldb + n), h, l);
-    th[ty + p][tx] = h;
-    tl[ty + p][tx] = l;
+  for (int p = 0; p < kTT / kTRows; ++p) {
+    const int k = k0 + ty + kTRows * p, n = n0 + tx;
+    v[p] = (k < K && n < N) ? __ldg(B + (long long)k * ldb + n) : 0.0f;
+  }
+#pragma unroll
+  for (int p = 0; p < kTT / kTRows; ++p) {
+    float h, l;
+    split1(v[p], h, l);
+    th[ty + kTRows * p][tx] = h;
+    tl[ty + kTRows * p][tx] = l;
   }
   __syncthreads();
 #pragma unroll
-  for (int p = 0; p < 32; p += 8) {
-    const int n = n0 + ty + p, k = k0 + tx;
+  for (int p = 0; p < kTT / kTRows; ++p) {
+    const int n = n0 + ty + kTRows * p, k = k0 + tx;
     if (n < N && k < K) {
-      hiT[(long long)n * kp + k] = th[tx][ty + p];
-      loT[(long long)n * kp + k] = tl[tx][ty + p];
+      hiT[(long long)n * kp + k] = th[tx][ty + kTRows * p];
+      loT[(long long)n * kp + k] = tl[tx][ty + kTRows * p];
     }
   }
 }
@@ -459,9 +467,11 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   split_rows_kernel<<<(unsigned)(M < (uint64_t)d.prof.sm_count * 8 ? M : (uint64_t)d.prof.sm_count * 8), 256, 0,
                       d.stream>>>(A, (long long)lda, (int)M,
                                                                                         (int)K, ahi, alo, (long long)kp); count_launch();
-  dim3 tg((unsigned)((N + 31) / 32), (unsigned)((K + 31) / 32));
+  dim3 tg((unsigned)((N + kTT - 1) / kTT), (unsigned)((K + kTT - 1) / kTT));
   if (tg.y > 65535) return set_error(MAPAL_ERR_UNSUPPORTED, "K too large for the split pass");
-  split_transpose_kernel<<<tg, dim3(32, 8), 0, d.stream>>>(B, (long long)ldb, (int)K, (int)N, bhi, blo, (long long)kp); count_launch();
+  split_transpose_kernel<<<tg, dim3(kTT, kTRows), 0, d.stream>>>(B, (long long)ldb, (int)K, (int)N, bhi, blo,
+                                                                (long long)kp);
+  count_launch();
 
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
   MAPAL_TRY(make_map(&m_ahi, ahi, M, K, kp, BM));

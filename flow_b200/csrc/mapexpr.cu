@@ -17,6 +17,12 @@
 namespace {
 
 constexpr int kMaxStack = 16;
+constexpr int kE = 4;         // elements per thread, advanced together op by op
+constexpr int kThreads = 256;
+// Internal form: a constant immediately followed by a binary op is folded
+// into the op (kImm + code, right operand in the op's immediate), so the
+// common "x * 7 + 13" shapes never touch the value stack.
+constexpr uint16_t kImm = 100;
 
 struct ExprProgram {
   MapalExprOp ops[MAPAL_X_MAX_OPS];
@@ -28,65 +34,146 @@ struct ExprProgram {
 __device__ __forceinline__ int32_t wrap_div(int32_t a, int32_t b) { return (a == INT32_MIN && b == -1) ? a : a / b; }
 __device__ __forceinline__ int32_t wrap_rem(int32_t a, int32_t b) { return b == -1 ? 0 : a % b; }
 
-__global__ void map_expr_kernel(const __grid_constant__ ExprProgram p, void* __restrict__ out, uint64_t n,
-                                unsigned* trap) {
-  for (uint64_t t = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; t < n; t += (uint64_t)gridDim.x * blockDim.x) {
-    uint32_t st[kMaxStack];
-    int sp = 0;
-    unsigned kind = 0;  // trap kind + 1
-    for (uint32_t pc = 0; pc < p.nops && !kind; ++pc) {
+// a OP b for a binary op code; *kind gets 1 (div_zero + 1) on a zero divisor.
+__device__ __forceinline__ uint32_t binop(uint16_t code, uint32_t aa, uint32_t bb, unsigned* kind) {
+  const int32_t ai = (int32_t)aa, bi = (int32_t)bb;
+  const float af = __uint_as_float(aa), bf = __uint_as_float(bb);
+  switch (code) {
+    case MAPAL_X_ADD_I32: return aa + bb;
+    case MAPAL_X_SUB_I32: return aa - bb;
+    case MAPAL_X_MUL_I32: return aa * bb;
+    case MAPAL_X_DIV_I32:
+      if (bi == 0) { *kind = 1; return 0u; }
+      return (uint32_t)wrap_div(ai, bi);
+    case MAPAL_X_REM_I32:
+      if (bi == 0) { *kind = 1; return 0u; }
+      return (uint32_t)wrap_rem(ai, bi);
+    case MAPAL_X_ADD_F32: return __float_as_uint(__fadd_rn(af, bf));
+    case MAPAL_X_SUB_F32: return __float_as_uint(__fsub_rn(af, bf));
+    case MAPAL_X_MUL_F32: return __float_as_uint(__fmul_rn(af, bf));
+    case MAPAL_X_DIV_F32: return __float_as_uint(__fdiv_rn(af, bf));
+    default: return __float_as_uint(fmodf(af, bf));  // MAPAL_X_REM_F32 (the host verified every code)
+  }
+}
+
+// Each thread advances kE elements, kThreads apart, through the program: the
+// op decode is shared by the elements, the top of the stack lives in
+// registers, and only deeper stack slots go to local memory. An element that
+// traps keeps its first trap kind, skips its later loads and is not stored.
+__global__ void __launch_bounds__(kThreads) map_expr_kernel(const __grid_constant__ ExprProgram p,
+                                                           void* __restrict__ out, uint64_t n, unsigned* trap) {
+  const uint64_t chunk = (uint64_t)kE * kThreads;
+  unsigned worst = 0;
+  for (uint64_t base = blockIdx.x * chunk; base < n; base += (uint64_t)gridDim.x * chunk) {
+    uint64_t tt[kE];
+    bool ok[kE];  // in the domain and not trapped
+    unsigned kind[kE];
+    uint32_t tos[kE];
+    uint32_t st[kMaxStack][kE];
+#pragma unroll
+    for (int e = 0; e < kE; ++e) {
+      tt[e] = base + (uint64_t)e * kThreads + threadIdx.x;
+      ok[e] = tt[e] < n;
+      kind[e] = 0;
+      tos[e] = 0;
+    }
+    int depth = 0;  // values on the stack, the top one in tos
+    for (uint32_t pc = 0; pc < p.nops; ++pc) {
       const MapalExprOp op = p.ops[pc];
+      if (op.code <= MAPAL_X_IN_F32) {  // pushes
+        if (depth > 0) {
+#pragma unroll
+          for (int e = 0; e < kE; ++e) st[depth - 1][e] = tos[e];
+        }
+        ++depth;
+#pragma unroll
+        for (int e = 0; e < kE; ++e) {
+          switch (op.code) {
+            case MAPAL_X_T_I32: tos[e] = (uint32_t)tt[e]; break;
+            case MAPAL_X_CONST_I32: tos[e] = (uint32_t)op.i; break;
+            case MAPAL_X_CONST_F32: tos[e] = __float_as_uint(op.f); break;
+            default:  // IN: slot verified on the host, and the array holds >= n elements
+              tos[e] = ok[e] ? __ldg(static_cast<const uint32_t*>(p.arrays[op.slot]) + tt[e]) : 0u;
+              break;
+          }
+        }
+        continue;
+      }
       switch (op.code) {
-        case MAPAL_X_T_I32: st[sp++] = (uint32_t)t; break;
-        case MAPAL_X_CONST_I32: st[sp++] = (uint32_t)op.i; break;
-        case MAPAL_X_CONST_F32: st[sp++] = __float_as_uint(op.f); break;
-        case MAPAL_X_IN_I32:
-        case MAPAL_X_IN_F32: st[sp++] = __ldg(static_cast<const uint32_t*>(p.arrays[op.slot]) + t); break;
         case MAPAL_X_LOAD_I32:
         case MAPAL_X_LOAD_F32: {
-          const int64_t j = (int64_t)(int32_t)st[sp - 1];
-          if (j < 0 || (uint64_t)j >= p.lens[op.slot]) {
-            kind = 2;  // index_oob
-            break;
+          const uint32_t* src = static_cast<const uint32_t*>(p.arrays[op.slot]);
+          const uint64_t len = p.lens[op.slot];
+#pragma unroll
+          for (int e = 0; e < kE; ++e) {
+            const int64_t j = (int64_t)(int32_t)tos[e];
+            uint32_t v = 0;
+            if (ok[e]) {
+              if (j < 0 || (uint64_t)j >= len) {
+                kind[e] = 2;  // index_oob
+                ok[e] = false;
+              } else {
+                v = __ldg(src + j);
+              }
+            }
+            tos[e] = v;
           }
-          st[sp - 1] = __ldg(static_cast<const uint32_t*>(p.arrays[op.slot]) + j);
           break;
         }
-        case MAPAL_X_NEG_I32: st[sp - 1] = (uint32_t)(0u - st[sp - 1]); break;
-        case MAPAL_X_NEG_F32: st[sp - 1] = __float_as_uint(-__uint_as_float(st[sp - 1])); break;
-        case MAPAL_X_WIDEN_I32_F32: st[sp - 1] = __float_as_uint(__int2float_rn((int32_t)st[sp - 1])); break;
+        case MAPAL_X_NEG_I32:
+#pragma unroll
+          for (int e = 0; e < kE; ++e) tos[e] = 0u - tos[e];
+          break;
+        case MAPAL_X_NEG_F32:
+#pragma unroll
+          for (int e = 0; e < kE; ++e) tos[e] ^= 0x80000000u;
+          break;
+        case MAPAL_X_WIDEN_I32_F32:
+#pragma unroll
+          for (int e = 0; e < kE; ++e) tos[e] = __float_as_uint(__int2float_rn((int32_t)tos[e]));
+          break;
         case MAPAL_X_STORE_I32:
-        case MAPAL_X_STORE_F32: static_cast<uint32_t*>(out)[t] = st[--sp]; break;
-        default: {
-          // binary ops: b on top, a below
-          const uint32_t bb = st[--sp], aa = st[sp - 1];
-          const int32_t ai = (int32_t)aa, bi = (int32_t)bb;
-          const float af = __uint_as_float(aa), bf = __uint_as_float(bb);
-          uint32_t r = 0;
-          switch (op.code) {
-            case MAPAL_X_ADD_I32: r = aa + bb; break;
-            case MAPAL_X_SUB_I32: r = aa - bb; break;
-            case MAPAL_X_MUL_I32: r = aa * bb; break;
-            case MAPAL_X_DIV_I32:
-              if (bi == 0) kind = 1; else r = (uint32_t)wrap_div(ai, bi);
-              break;
-            case MAPAL_X_REM_I32:
-              if (bi == 0) kind = 1; else r = (uint32_t)wrap_rem(ai, bi);
-              break;
-            case MAPAL_X_ADD_F32: r = __float_as_uint(__fadd_rn(af, bf)); break;
-            case MAPAL_X_SUB_F32: r = __float_as_uint(__fsub_rn(af, bf)); break;
-            case MAPAL_X_MUL_F32: r = __float_as_uint(__fmul_rn(af, bf)); break;
-            case MAPAL_X_DIV_F32: r = __float_as_uint(__fdiv_rn(af, bf)); break;
-            case MAPAL_X_REM_F32: r = __float_as_uint(fmodf(af, bf)); break;
-            default: kind = 3; break;  // unreachable: the host verified every code
-          }
-          st[sp - 1] = r;
+        case MAPAL_X_STORE_F32:
+#pragma unroll
+          for (int e = 0; e < kE; ++e)
+            if (ok[e]) static_cast<uint32_t*>(out)[tt[e]] = tos[e];
           break;
-        }
+        default:
+          if (op.code >= kImm) {  // tos OP immediate
+            const uint16_t code = op.code - kImm;
+            const uint32_t imm = code >= MAPAL_X_ADD_F32 ? __float_as_uint(op.f) : (uint32_t)op.i;
+#pragma unroll
+            for (int e = 0; e < kE; ++e) {
+              unsigned k = 0;
+              tos[e] = binop(code, tos[e], imm, &k);
+              if (k && ok[e]) {
+                kind[e] = k;
+                ok[e] = false;
+              }
+            }
+          } else {  // st[depth-2] OP tos
+            --depth;
+#pragma unroll
+            for (int e = 0; e < kE; ++e) {
+              unsigned k = 0;
+              tos[e] = binop(op.code, st[depth - 1][e], tos[e], &k);
+              if (k && ok[e]) {
+                kind[e] = k;
+                ok[e] = false;
+              }
+            }
+          }
+          break;
       }
     }
-    if (kind) atomicMax(trap, kind);
+#pragma unroll
+    for (int e = 0; e < kE; ++e) worst = kind[e] > worst ? kind[e] : worst;
   }
+  if (worst) atomicMax(trap, worst);
+}
+
+bool is_binary(uint16_t c) {
+  return (c >= MAPAL_X_ADD_I32 && c <= MAPAL_X_REM_I32) || (c >= MAPAL_X_ADD_F32 && c <= MAPAL_X_REM_F32);
 }
 
 // Host check: every op known, operand types consistent, stack within bounds,
@@ -158,8 +245,22 @@ extern "C" int mapal_gpu_map_expr(MapalGpuCtx* ctx, const MapalExprOp* prog, uin
   if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
   if (n > (1ull << 31)) return set_error(MAPAL_ERR_UNSUPPORTED, "index domain beyond i32");
   ExprProgram p{};
-  for (uint32_t i = 0; i < nops; ++i) p.ops[i] = prog[i];
-  p.nops = nops;
+  uint32_t m = 0;
+  for (uint32_t i = 0; i < nops; ++i) {
+    const uint16_t c = prog[i].code;
+    const bool is_const = c == MAPAL_X_CONST_I32 || c == MAPAL_X_CONST_F32;
+    if (is_const && i + 1 < nops && is_binary(prog[i + 1].code)) {
+      p.ops[m] = prog[i + 1];
+      p.ops[m].code = (uint16_t)(kImm + prog[i + 1].code);
+      p.ops[m].i = prog[i].i;
+      p.ops[m].f = prog[i].f;
+      ++m;
+      ++i;
+    } else {
+      p.ops[m++] = prog[i];
+    }
+  }
+  p.nops = m;
   for (uint32_t s = 0; s < narrays; ++s) {
     p.arrays[s] = arrays[s];
     p.lens[s] = lens[s];
@@ -170,7 +271,8 @@ extern "C" int mapal_gpu_map_expr(MapalGpuCtx* ctx, const MapalExprOp* prog, uin
     if ((prog[i].code == MAPAL_X_IN_I32 || prog[i].code == MAPAL_X_IN_F32) && lens[prog[i].slot] < n)
       return set_error(MAPAL_ERR_INVALID, "a mapped input is shorter than the domain");
   DeviceSlot& d = ctx->dev[0];
-  map_expr_kernel<<<stream_grid(n, 256, d.prof.sm_count, 8), 256, 0, d.stream>>>(p, out, n, d.trap);
+  map_expr_kernel<<<stream_grid((n + kE - 1) / kE, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(
+      p, out, n, d.trap);
   count_launch();
   return finish(ctx, 0, true);
 }

@@ -20,7 +20,7 @@ import math
 
 import flow_b200 as fb
 
-SITES = ("saxpy", "transpose", "gather", "sum", "fir", "conv2d", "matmul")
+SITES = ("saxpy", "transpose", "gather", "sum", "fir", "conv2d", "matmul", "map_expr")
 
 
 def _alloc(torch, n, dtype=None):
@@ -104,6 +104,19 @@ def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = f
         per = 4 * (2 * n * kk + n * n)
         run = lambda s: ctx.matmul(site, s[0], s[1], s[2], mode)
         flops = 2 * n * n * kk
+    elif name == "map_expr":
+        # the benches' generator body as a general map program:
+        # t -> (t * 7 + 13) % 101 - 50 -> widen_f32
+        from .records import program
+        prog = program(("T_I32",), ("CONST_I32", 7), ("MUL_I32",), ("CONST_I32", 13), ("ADD_I32",),
+                       ("CONST_I32", 101), ("REM_I32",), ("CONST_I32", 50), ("SUB_I32",), ("WIDEN_I32_F32",),
+                       ("STORE_F32",))
+
+        def mk(i):
+            return (_alloc(torch, n),)
+        per = 4 * n
+        run = lambda s: ctx.map_expr(prog, [], s[0], n)
+        flops = 0
     else:
         raise ValueError(f"unknown site {name}")
     return mk, run, per, flops
@@ -175,7 +188,7 @@ def main() -> int:
     args = ap.parse_args()
     import torch
     defaults = {"saxpy": 1 << 20, "transpose": 1024 * 1024, "gather": 1 << 20, "sum": 1 << 20,
-                "fir": 1 << 20, "conv2d": 1024 * 1024, "matmul": 4096}
+                "fir": 1 << 20, "conv2d": 1024 * 1024, "matmul": 4096, "map_expr": 1 << 20}
     sites = SITES if args.site == "all" else (args.site,)
     with fb.Context((0,), sync=False) as ctx:
         l2 = ctx.profile().l2_bytes

@@ -11,8 +11,9 @@
 //
 //   N -> iota                          an index domain (never materialised)
 //   dom -> map { t -> body }           a recognised site (matmul / FIR / conv
-//                                      tile sites, move sites, gather, saxpy) or
-//                                      else the general map body program
+//                                      tile sites, move sites, gather, saxpy,
+//                                      the affine integer generator) or else
+//                                      the general map body program
 //   (x, y) -> zip -> map { p -> ... }  zipped inputs
 //   (seed, xs) -> fold { acc, v -> acc + v }   the sum fold
 //   a[i] -> println, "text" -> print, () -> time, scalar arithmetic
@@ -776,8 +777,43 @@ struct Runner {
       if (Value r; try_gather(L.params[0], body, dom, r, line)) return r;
       if (Value r; try_move(L.params[0], body, dom, r, line)) return r;
       if (Value r; try_saxpy(L.params[0], body, dom, r, line)) return r;
+    } else {
+      if (Value r; try_affine_gen(L.params[0], body, dom, r, line)) return r;
     }
     return general_map(L.params[0], body, widen, dom, line);
+  }
+
+  // t -> (t * A + B) % M - C -> widen_f32 over an index domain, integer
+  // literals with M > 0: the benches' integer generators, one fused kernel.
+  bool try_affine_gen(const std::string& prm, const EP& b, const Value& dom, Value& out, int line) {
+    (void)line;
+    if (dom.ty != TY_IOTA) return false;
+    auto lit = [](const EP& e, long long& v) {
+      if (e->k != Expr::INT || e->ival < INT32_MIN || e->ival > INT32_MAX) return false;
+      v = e->ival;
+      return true;
+    };
+    auto bin = [](const EP& e, char op) { return e->k == Expr::BIN && e->op == op; };
+    long long A, B, M, C;
+    if (!bin(b, '-') || !lit(b->kids[1], C)) return false;
+    const EP& rem = b->kids[0];
+    if (!bin(rem, '%') || !lit(rem->kids[1], M) || M <= 0) return false;
+    const EP& add = rem->kids[0];
+    if (!bin(add, '+') || !lit(add->kids[1], B)) return false;
+    const EP& mul = add->kids[0];
+    if (!bin(mul, '*')) return false;
+    const EP &x = mul->kids[0], &y = mul->kids[1];
+    const bool t_first = x->k == Expr::NAME && x->s == prm && lit(y, A);
+    const bool t_second = y->k == Expr::NAME && y->s == prm && lit(x, A);
+    if (!t_first && !t_second) return false;
+    say("gen_affine n=" + std::to_string(dom.n) + " mul=" + std::to_string(A) + " add=" + std::to_string(B) +
+        " mod=" + std::to_string(M) + " sub=" + std::to_string(C));
+    out = make_array(TY_F32, dom.n);
+    if (!plan)
+      check(mapal_gpu_gen_affine_f32(ctx, (float*)out.ptr(), dom.n, 0, (int32_t)A, (int32_t)B, (int32_t)M,
+                                     (int32_t)C),
+            "gen_affine");
+    return true;
   }
 
   // j -> x[j] over an i32 array

@@ -97,3 +97,44 @@ def test_malformed_programs_rejected(ctx):
                 P(("IN_F32", 3), ("STORE_F32",))]:                   # slot beyond the table
         with pytest.raises(fb.MapalInfraError):
             ctx.map_expr(bad, [], empty_f32(4))
+
+
+@pytest.mark.parametrize("n", [1, 3, 1023, 1025, 4097, 100001])
+def test_ragged_domains_and_deep_stack(ctx, n):
+    # ((t+1)*(t+2) + (t+3)*(t+4)) * ((t+5) - (t+6)*(t+7)) -> widen, with every
+    # product's operands pushed first: the stack reaches depth 5, so values
+    # below the top go through the spill slots; n exercises partial chunks.
+    prog = P(("T_I32",), ("CONST_I32", 1), ("ADD_I32",), ("T_I32",), ("CONST_I32", 2), ("ADD_I32",),
+             ("MUL_I32",), ("T_I32",), ("CONST_I32", 3), ("ADD_I32",), ("T_I32",), ("CONST_I32", 4),
+             ("ADD_I32",), ("MUL_I32",), ("ADD_I32",), ("T_I32",), ("CONST_I32", 5), ("ADD_I32",),
+             ("T_I32",), ("CONST_I32", 6), ("ADD_I32",), ("T_I32",), ("CONST_I32", 7), ("ADD_I32",),
+             ("MUL_I32",), ("SUB_I32",), ("MUL_I32",), ("WIDEN_I32_F32",), ("STORE_F32",))
+    got, want = run_both(ctx, prog, [], n)
+    assert same_bits(got, want)
+
+
+def test_constant_operands_in_both_positions(ctx):
+    # 2.5 / x - (1.5 * 0.75) and 7 - t % 5: a constant as the left operand
+    # stays a stack value; one right after another operand folds into the op
+    n = 3001
+    x = o.gen(n, 5, 0)
+    prog = P(("CONST_F32", 2.5), ("IN_F32", 0), ("DIV_F32",), ("CONST_F32", 1.5), ("CONST_F32", 0.75),
+             ("MUL_F32",), ("SUB_F32",), ("STORE_F32",))
+    got, want = run_both(ctx, prog, [x], n)
+    assert same_bits(got, want)
+    prog = P(("CONST_I32", 7), ("T_I32",), ("CONST_I32", 5), ("REM_I32",), ("SUB_I32",), ("STORE_I32",))
+    got, want = run_both(ctx, prog, [], n, out_i32=True)
+    assert np.array_equal(got, want)
+
+
+def test_trap_in_a_few_elements_of_many(ctx):
+    # only elements t = 999999 and beyond read past the array: index_oob
+    n = 1 << 20
+    a = o.gen(999999, 6, 0)
+    prog = P(("T_I32",), ("LOAD_F32", 0), ("STORE_F32",))
+    with pytest.raises(fb.MapalTrap) as e:
+        ctx.map_expr(prog, [dev(a)], empty_f32(n))
+    assert e.value.kind == "index_oob"
+    ok = empty_f32(999999)
+    ctx.map_expr(prog, [dev(a)], ok)
+    assert same_bits(host(ok), a)

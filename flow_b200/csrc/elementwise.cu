@@ -140,9 +140,13 @@ __global__ void gather_scalar_kernel(const float* __restrict__ x, int64_t n_x,
 }
 
 // Transpose-shaped move site (cq == 1): out[r][w] = in[w*cr + r] for an
-// output of `rows` x `width`. 32x32 tiles through shared memory padded to
-// 33 columns, so both the read (along r) and the write (along w) coalesce.
-constexpr int kTile = 32, kRowsPerPass = 8;
+// output of `rows` x `width`. Square tiles through shared memory padded by
+// one column, so both the read (along r) and the write (along w) coalesce;
+// each thread issues all of its loads before its first shared store. Large
+// sites use 64x64 tiles (64x4 threads; 0.81-0.82 of the copy rate at 4096^2
+// and 8192^2 on B200 against 0.69-0.72 with 32x32), small ones 32x32 tiles
+// (32x8 threads: at 1024^2 the 64x64 grid is too short to fill the SMs).
+template <int kTile, int kRowsPerPass>
 __global__ void __launch_bounds__(kTile* kRowsPerPass) transpose_kernel(const float* __restrict__ in,
                                                                         float* __restrict__ out,
                                                                         uint64_t rows, uint64_t width,
@@ -151,17 +155,31 @@ __global__ void __launch_bounds__(kTile* kRowsPerPass) transpose_kernel(const fl
   const uint64_t r0 = (uint64_t)blockIdx.x * kTile;  // output row block (input column block)
   const uint64_t w0 = (uint64_t)blockIdx.y * kTile;  // output column block (input row block)
   const int tx = threadIdx.x, ty = threadIdx.y;
+  float v[kTile / kRowsPerPass];
 #pragma unroll
-  for (int p = 0; p < kTile; p += kRowsPerPass) {
-    uint64_t w = w0 + ty + p, r = r0 + tx;
-    if (w < width && r < rows) tile[ty + p][tx] = __ldcs(in + w * cr + r);
+  for (int p = 0; p < kTile / kRowsPerPass; ++p) {
+    const uint64_t w = w0 + ty + kRowsPerPass * p, r = r0 + tx;
+    v[p] = (w < width && r < rows) ? __ldcs(in + w * cr + r) : 0.0f;
   }
+#pragma unroll
+  for (int p = 0; p < kTile / kRowsPerPass; ++p) tile[ty + kRowsPerPass * p][tx] = v[p];
   __syncthreads();
 #pragma unroll
-  for (int p = 0; p < kTile; p += kRowsPerPass) {
-    uint64_t r = r0 + ty + p, w = w0 + tx;
-    if (r < rows && w < width) __stcs(out + r * width + w, tile[tx][ty + p]);
+  for (int p = 0; p < kTile / kRowsPerPass; ++p) {
+    const uint64_t r = r0 + ty + kRowsPerPass * p, w = w0 + tx;
+    if (r < rows && w < width) __stcs(out + r * width + w, tile[tx][ty + kRowsPerPass * p]);
   }
+}
+
+template <int kTile, int kRowsPerPass>
+int launch_transpose(cudaStream_t s, const float* in, float* out, uint64_t rows, uint64_t width, uint64_t cr) {
+  dim3 grid((unsigned)((rows + kTile - 1) / kTile), (unsigned)((width + kTile - 1) / kTile));
+  if (grid.y > 65535 || (rows + kTile - 1) / kTile > 0x7fffffffull)
+    return set_error(MAPAL_ERR_UNSUPPORTED, "transpose too large");
+  transpose_kernel<kTile, kRowsPerPass><<<grid, dim3(kTile, kRowsPerPass), 0, s>>>(in, out, rows, width, cr);
+  count_launch();
+  return 0;
+}
 }
 
 // Any other move site: one thread per output element (addresses validated
@@ -282,9 +300,10 @@ extern "C" int mapal_gpu_transpose(MapalGpuCtx* ctx, const MapalMoveSite* site, 
   if (max_addr >= site->len) return set_error(MAPAL_TRAP_INDEX_OOB, "mapal trap: index_oob");
   DeviceSlot& d = ctx->dev[0];
   if (site->cq == 1) {
-    dim3 grid((unsigned)((rows + kTile - 1) / kTile), (unsigned)((width + kTile - 1) / kTile));
-    if (grid.y > 65535) return set_error(MAPAL_ERR_UNSUPPORTED, "transpose width too large");
-    transpose_kernel<<<grid, dim3(kTile, kRowsPerPass), 0, d.stream>>>(in, out, rows, width, site->cr); count_launch();
+    if (rows * width >= (4ull << 20))
+      MAPAL_TRY((launch_transpose<64, 4>(d.stream, in, out, rows, width, site->cr)));
+    else
+      MAPAL_TRY((launch_transpose<32, 8>(d.stream, in, out, rows, width, site->cr)));
   } else {
     uint64_t n = rows * width;
     move_generic_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(

@@ -180,7 +180,6 @@ int launch_transpose(cudaStream_t s, const float* in, float* out, uint64_t rows,
   count_launch();
   return 0;
 }
-}
 
 // Any other move site: one thread per output element (addresses validated
 // on the host, so no guard is needed).

@@ -13,8 +13,8 @@
 //
 // Each thread computes pairs of outputs half a tile apart as packed values
 // (f32x2.cuh): FIR forms both rounded products with one packed FMA whose
-// addend is a run-time -0.0; conv2d uses two scalar rounded products; both
-// accumulate with one packed rounded add.
+// addend is a run-time -0.0 (so does conv2d); both accumulate with one packed
+// rounded add.
 #include "common.cuh"
 #include "cpasync.cuh"
 #include "f32x2.cuh"
@@ -121,70 +121,93 @@ __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restric
 
 // ---- conv2d 3x3 ---------------------------------------------------------------
 
-constexpr int kConvThreads = 64;         // one thread per column pair
-constexpr int kConvHalf = kConvThreads;  // column pairs per block -> 128 columns
-constexpr int kConvP = 8;                // output rows per thread
-constexpr int kConvCols = 2 * kConvHalf;
-constexpr int kConvPitch = kConvCols + 4;  // 130 used, 16-byte rows
+constexpr int kConvThreads = 128;             // one thread per column pair (c, c + 128)
+constexpr int kConvHalf = kConvThreads;
+constexpr int kConvCols = 2 * kConvHalf;           // output columns per block
+constexpr int kConvPitch = kConvCols + 8;          // 258 used after an alignment shift of up to 3
+constexpr int kConvChunks = (kConvCols + 2 + 3 + 3) / 4;  // 16-byte chunks that cover a staged row
 
-// out[i, j] = fold_k(acc + w[k] * img[(i + k/3)*stride + j + k%3]) from seed.
+// Shift (in floats) of a row's first needed element above the 16-byte
+// boundary below it: the staged row starts at that boundary.
+__device__ __forceinline__ int conv_shift(const float* p) { return (int)(((uintptr_t)p >> 2) & 3); }
+
+// out[i, j] = fold_k(acc + w[k] * img[(i + k/3)*stride + j + k%3]) from seed,
+// for a strip of P output rows x kConvCols columns. The P + 2 input rows are
+// staged by 16-byte cp.async whatever the stride (elements outside the needed
+// span are zero-filled and never read); each thread then walks the rows once,
+// keeping P packed accumulators for its two columns, and every MAC pair is one
+// packed FMA with a run-time -0.0 addend plus one packed add (f32x2.cuh).
+template <int P>
 __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __restrict__ w,
                                                                const float* __restrict__ img,
                                                                uint64_t img_len, uint64_t stride,
                                                                float* __restrict__ out, uint64_t rows,
-                                                               uint64_t cols, float seed) {
-  __shared__ __align__(16) float tile[kConvP + 2][kConvPitch];
-  const uint64_t i0 = (uint64_t)blockIdx.y * kConvP;
+                                                               uint64_t cols, float seed, float neg_zero) {
+  __shared__ __align__(16) float tile[P + 2][kConvPitch];
+  const uint64_t i0 = (uint64_t)blockIdx.y * P;
   const uint64_t j0 = (uint64_t)blockIdx.x * kConvCols;
-  const bool al = ((uintptr_t)img & 15) == 0 && (stride & 3) == 0;
-  constexpr int kChunks = kConvPitch / 4;
-  for (int e = threadIdx.x; e < (kConvP + 2) * kChunks; e += kConvThreads) {
-    const int r = e / kChunks, c = 4 * (e % kChunks);
-    const uint64_t row = i0 + r, col = j0 + c;
-    int nvalid = 0;
-    uint64_t g = 0;
-    if (row < rows + 2 && col < cols + 2) {
-      g = row * stride + col;
-      const uint64_t lim_row = cols + 2 - col, lim_len = g < img_len ? img_len - g : 0;
-      const uint64_t lim = lim_row < lim_len ? lim_row : lim_len;
-      nvalid = (int)(lim < 4 ? lim : 4);
+  const uint64_t need = cols + 2 - j0 < (uint64_t)(kConvCols + 2) ? cols + 2 - j0 : (uint64_t)(kConvCols + 2);
+  const float* const img_end = img + img_len;
+  const float* rowp = img + i0 * stride + j0;  // first needed element of staged row r
+  int sh[P + 2];                               // each staged row's alignment shift
+#pragma unroll
+  for (int r = 0; r < P + 2; ++r, rowp += stride) {
+    sh[r] = conv_shift(rowp);
+    if (i0 + r >= rows + 2) continue;  // feeds no stored output: left unstaged
+    const float* lo = rowp - sh[r];
+    const float* hi = rowp + need < img_end ? rowp + need : img_end;
+    for (int ch = threadIdx.x; ch < kConvChunks; ch += kConvThreads) {
+      const float* e0 = lo + 4 * ch;
+      const uint32_t dst = smem_u32(&tile[r][4 * ch]);
+      if (e0 >= rowp && e0 + 4 <= hi) {
+        cp_async16(dst, e0, true);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const bool ok = e0 + q >= rowp && e0 + q < hi;
+          cp_async4(dst + 4 * q, ok ? e0 + q : img, ok);
+        }
+      }
     }
-    copy4(smem_u32(&tile[r][c]), img + (nvalid > 0 ? g : 0), nvalid, al);
   }
   cp_commit();
-  float w9[9];
+  f2 w9[9];
 #pragma unroll
-  for (int k = 0; k < 9; ++k) w9[k] = __ldg(w + k);
+  for (int k = 0; k < 9; ++k) w9[k] = f2_splat(__ldg(w + k));
+  const f2 z2 = f2_splat(neg_zero);  // -0.0, unknown to the compiler: see f2_mac_z
   cp_wait<0>();
   __syncthreads();
 
   const int c = threadIdx.x;
-  f2 acc[kConvP];
+  f2 acc[P];
   const f2 s2 = f2_splat(seed);
 #pragma unroll
-  for (int p = 0; p < kConvP; ++p) acc[p] = s2;
+  for (int p = 0; p < P; ++p) acc[p] = s2;
   // Input row r feeds output rows r-2..r (tap rows 2..0); walking r upward
   // applies each output's taps in ascending k (k = 3*dr + dc, dr = r - p).
 #pragma unroll
-  for (int r = 0; r < kConvP + 2; ++r) {
-    const float a0 = tile[r][c], a1 = tile[r][c + 1], a2 = tile[r][c + 2];
-    const float b0 = tile[r][kConvHalf + c], b1 = tile[r][kConvHalf + c + 1], b2 = tile[r][kConvHalf + c + 2];
+  for (int r = 0; r < P + 2; ++r) {
+    const float* tr = &tile[r][sh[r] + c];
+    const f2 x0 = f2_pack(tr[0], tr[kConvHalf]), x1 = f2_pack(tr[1], tr[kConvHalf + 1]),
+             x2 = f2_pack(tr[2], tr[kConvHalf + 2]);
 #pragma unroll
     for (int dr = 0; dr < 3; ++dr) {
       const int p = r - dr;
-      if (p >= 0 && p < kConvP) {
-        acc[p] = f2_mac(acc[p], w9[3 * dr + 0], a0, w9[3 * dr + 0], b0);
-        acc[p] = f2_mac(acc[p], w9[3 * dr + 1], a1, w9[3 * dr + 1], b1);
-        acc[p] = f2_mac(acc[p], w9[3 * dr + 2], a2, w9[3 * dr + 2], b2);
+      if (p >= 0 && p < P) {
+        acc[p] = f2_mac_z(acc[p], w9[3 * dr + 0], x0, z2);
+        acc[p] = f2_mac_z(acc[p], w9[3 * dr + 1], x1, z2);
+        acc[p] = f2_mac_z(acc[p], w9[3 * dr + 2], x2, z2);
       }
     }
   }
+  const uint64_t ja = j0 + c, jb = j0 + kConvHalf + c;
+  const bool oka = ja < cols, okb = jb < cols;
+  float* orow = out + i0 * cols + ja;
 #pragma unroll
-  for (int p = 0; p < kConvP; ++p) {
-    const uint64_t i = i0 + p, ja = j0 + c, jb = j0 + kConvHalf + c;
-    if (i < rows) {
-      if (ja < cols) out[i * cols + ja] = f2_lo(acc[p]);
-      if (jb < cols) out[i * cols + jb] = f2_hi(acc[p]);
+  for (int p = 0; p < P; ++p, orow += cols) {
+    if (i0 + p < rows) {
+      if (oka) __stcs(orow, f2_lo(acc[p]));
+      if (okb) __stcs(orow + kConvHalf, f2_hi(acc[p]));
     }
   }
 }
@@ -212,11 +235,22 @@ int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, ui
   return 0;
 }
 
-int launch_conv3x3(cudaStream_t s, const float* w, const float* img, uint64_t img_len, uint64_t stride,
+int launch_conv3x3(cudaStream_t s, int sms, const float* w, const float* img, uint64_t img_len, uint64_t stride,
                    float* out, uint64_t rows, uint64_t cols, float seed) {
-  dim3 grid((unsigned)((cols + kConvCols - 1) / kConvCols), (unsigned)((rows + kConvP - 1) / kConvP));
-  if ((cols + kConvCols - 1) / kConvCols > 0x7fffffffull || (rows + kConvP - 1) / kConvP > 65535)
-    return MAPAL_ERR_UNSUPPORTED;
-  conv3x3_kernel<<<grid, kConvThreads, 0, s>>>(w, img, img_len, stride, out, rows, cols, seed); count_launch();
+  const uint64_t bx = (cols + kConvCols - 1) / kConvCols;
+  if (bx > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
+  // 8-row strips when they give every SM a few blocks, 4-row strips
+  // otherwise (B200, 4098^2 and 8194^2 images: 8 rows beat 4, 16 and 32 by
+  // 3-40 %; at 1026^2 4 rows win: the grid is the limit there).
+  const uint64_t by8 = (rows + 7) / 8, by4 = (rows + 3) / 4;
+  if (bx * by8 >= 4ull * (uint64_t)sms && by8 <= 65535) {
+    conv3x3_kernel<8><<<dim3((unsigned)bx, (unsigned)by8), kConvThreads, 0, s>>>(w, img, img_len, stride, out, rows,
+                                                                                 cols, seed, -0.0f);
+  } else {
+    if (by4 > 65535) return MAPAL_ERR_UNSUPPORTED;
+    conv3x3_kernel<4><<<dim3((unsigned)bx, (unsigned)by4), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
+                                                                                 rows, cols, seed, -0.0f);
+  }
+  count_launch();
   return 0;
 }

@@ -133,7 +133,7 @@ __device__ __forceinline__ int conv_shift(const float* p) { return (int)(((uintp
 
 // out[i, j] = fold_k(acc + w[k] * img[(i + k/3)*stride + j + k%3]) from seed,
 // for a strip of P output rows x kConvCols columns. The P + 2 input rows are
-// staged by 16-byte cp.async whatever the stride (elements outside the needed
+// staged (a warp per row) by 16-byte cp.async whatever the stride (elements outside the needed
 // span are zero-filled and never read); each thread then walks the rows once,
 // keeping P packed accumulators for its two columns, and every MAC pair is one
 // packed FMA with a run-time -0.0 addend plus one packed add (f32x2.cuh).
@@ -148,15 +148,18 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
   const uint64_t j0 = (uint64_t)blockIdx.x * kConvCols;
   const uint64_t need = cols + 2 - j0 < (uint64_t)(kConvCols + 2) ? cols + 2 - j0 : (uint64_t)(kConvCols + 2);
   const float* const img_end = img + img_len;
-  const float* rowp = img + i0 * stride + j0;  // first needed element of staged row r
-  int sh[P + 2];                               // each staged row's alignment shift
-#pragma unroll
-  for (int r = 0; r < P + 2; ++r, rowp += stride) {
-    sh[r] = conv_shift(rowp);
+  __shared__ int shs[P + 2];  // each staged row's alignment shift
+  // Staging: warp w takes rows w, w + 4, ...; its lanes take the row's chunks
+  // (one row's setup per warp, not per thread).
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int r = warp; r < P + 2; r += kConvThreads / 32) {
+    const float* rowp = img + (i0 + r) * stride + j0;  // first needed element of staged row r
+    const int sh = conv_shift(rowp);
+    if (lane == 0) shs[r] = sh;
     if (i0 + r >= rows + 2) continue;  // feeds no stored output: left unstaged
-    const float* lo = rowp - sh[r];
+    const float* lo = rowp - sh;
     const float* hi = rowp + need < img_end ? rowp + need : img_end;
-    for (int ch = threadIdx.x; ch < kConvChunks; ch += kConvThreads) {
+    for (int ch = lane; ch < kConvChunks; ch += 32) {
       const float* e0 = lo + 4 * ch;
       const uint32_t dst = smem_u32(&tile[r][4 * ch]);
       if (e0 >= rowp && e0 + 4 <= hi) {
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
   // applies each output's taps in ascending k (k = 3*dr + dc, dr = r - p).
 #pragma unroll
   for (int r = 0; r < P + 2; ++r) {
-    const float* tr = &tile[r][sh[r] + c];
+    const float* tr = &tile[r][shs[r] + c];
     const f2 x0 = f2_pack(tr[0], tr[kConvHalf]), x1 = f2_pack(tr[1], tr[kConvHalf + 1]),
              x2 = f2_pack(tr[2], tr[kConvHalf + 2]);
 #pragma unroll
@@ -239,13 +242,13 @@ int launch_conv3x3(cudaStream_t s, int sms, const float* w, const float* img, ui
                    float* out, uint64_t rows, uint64_t cols, float seed) {
   const uint64_t bx = (cols + kConvCols - 1) / kConvCols;
   if (bx > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
-  // 8-row strips when they give every SM a few blocks, 4-row strips
-  // otherwise (B200, 4098^2 and 8194^2 images: 8 rows beat 4, 16 and 32 by
-  // 3-40 %; at 1026^2 4 rows win: the grid is the limit there).
-  const uint64_t by8 = (rows + 7) / 8, by4 = (rows + 3) / 4;
-  if (bx * by8 >= 4ull * (uint64_t)sms && by8 <= 65535) {
-    conv3x3_kernel<8><<<dim3((unsigned)bx, (unsigned)by8), kConvThreads, 0, s>>>(w, img, img_len, stride, out, rows,
-                                                                                 cols, seed, -0.0f);
+  // 16-row strips when they give every SM a few blocks, 4-row strips
+  // otherwise (B200, 4098^2 and 8194^2 images: 16 rows beat 4, 8 and 32 by
+  // 4-25 %; at 1026^2 4 rows win: the grid is the limit there).
+  const uint64_t by16 = (rows + 15) / 16, by4 = (rows + 3) / 4;
+  if (bx * by16 >= 4ull * (uint64_t)sms && by16 <= 65535) {
+    conv3x3_kernel<16><<<dim3((unsigned)bx, (unsigned)by16), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
+                                                                                   rows, cols, seed, -0.0f);
   } else {
     if (by4 > 65535) return MAPAL_ERR_UNSUPPORTED;
     conv3x3_kernel<4><<<dim3((unsigned)bx, (unsigned)by4), kConvThreads, 0, s>>>(w, img, img_len, stride, out,

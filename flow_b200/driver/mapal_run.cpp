@@ -73,7 +73,8 @@ void check(int rc, const char* what) {
 // ---- lexer -----------------------------------------------------------------------------
 
 enum Tok { T_EOF, T_IDENT, T_INT, T_FLOAT, T_STR, T_ARROW, T_LBRACE, T_RBRACE, T_LPAREN, T_RPAREN, T_LBRACK,
-           T_RBRACK, T_COMMA, T_SEMI, T_COLON, T_DOT, T_PLUS, T_MINUS, T_STAR, T_SLASH, T_PERCENT, T_OTHER };
+           T_RBRACK, T_COMMA, T_SEMI, T_COLON, T_DOT, T_PLUS, T_MINUS, T_STAR, T_SLASH, T_PERCENT, T_LT, T_LARROW,
+           T_OTHER };
 
 struct Token {
   Tok k;
@@ -135,6 +136,11 @@ std::vector<Token> lex(const std::string& src) {
       i += 2;
       continue;
     }
+    if (c == '<' && i + 1 < src.size() && src[i + 1] == '-') {
+      out.push_back({T_LARROW, "<-", line});
+      i += 2;
+      continue;
+    }
     Tok k = T_OTHER;
     switch (c) {
       case '{': k = T_LBRACE; break;
@@ -152,6 +158,7 @@ std::vector<Token> lex(const std::string& src) {
       case '*': k = T_STAR; break;
       case '/': k = T_SLASH; break;
       case '%': k = T_PERCENT; break;
+      case '<': k = T_LT; break;
       default: break;
     }
     out.push_back({k, std::string(1, c), line});
@@ -192,9 +199,35 @@ struct Chain {
   int line = 0;
 };
 
+// A helper function in the counted-loop form the reference lifts into a
+// Fold or a Map (crates/mapal-rewrite/src/lift.rs:1-12):
+//   mut CTR: i32 <- 0; mut X: T <- init;
+//   loop { (CTR < K) -> { -true-> { stmts; CTR + 1 -> CTR; -> loop; } -false-> X -> ret; } }
+struct LoopStmt {
+  enum K { BIND, UPDATE } k;
+  Chain chain;       // BIND: `expr [-> f] -> name`
+  EP target, value;  // UPDATE: `target[idx] <- value` (target is the INDEX expression)
+};
+
+struct FnDef {
+  std::string name;
+  std::vector<std::string> params;
+  struct Mut {
+    std::string name;
+    long long arr_len = -1;  // array length from the type, -1 for a scalar
+    EP init;
+  };
+  std::vector<Mut> muts;
+  EP cond_lhs, cond_rhs;        // (cond_lhs < cond_rhs)
+  std::vector<LoopStmt> body;   // the true branch, without `-> loop`
+  EP ret;                       // the false branch's value
+  int line = 0;
+};
+
 struct Parser {
   std::vector<Token> t;
   size_t p = 0;
+  std::map<std::string, FnDef> fns;
 
   const Token& cur() const { return t[p]; }
   bool at(Tok k) const { return t[p].k == k; }
@@ -383,6 +416,107 @@ struct Parser {
     return c;
   }
 
+  // `name: T` with T a scalar type or `[T; N]`; returns N for arrays, else -1
+  long long param_type() {
+    if (at(T_LBRACK)) {
+      ++p;
+      take(T_IDENT, "element type");
+      take(T_SEMI, "';'");
+      const long long n = atoll(take(T_INT, "array length").s.c_str());
+      take(T_RBRACK, "']'");
+      return n;
+    }
+    take(T_IDENT, "type");
+    return -1;
+  }
+
+  FnDef loop_fn(const std::string& name, int line) {
+    FnDef f;
+    f.name = name;
+    f.line = line;
+    take(T_LPAREN, "'('");
+    while (!at(T_RPAREN)) {
+      f.params.push_back(take(T_IDENT, "parameter").s);
+      take(T_COLON, "':'");
+      param_type();
+      if (at(T_COMMA)) ++p;
+    }
+    take(T_RPAREN, "')'");
+    if (at(T_ARROW)) {
+      ++p;
+      param_type();
+    }
+    take(T_LBRACE, "'{'");
+    while (at(T_IDENT) && cur().s == "mut") {
+      ++p;
+      FnDef::Mut m;
+      m.name = take(T_IDENT, "name").s;
+      take(T_COLON, "':'");
+      m.arr_len = param_type();
+      take(T_LARROW, "'<-'");
+      m.init = expr();
+      take(T_SEMI, "';'");
+      f.muts.push_back(m);
+    }
+    auto kw = [&](const char* w) {
+      Token k = take(T_IDENT, w);
+      if (k.s != w) unsupported("line %d: expected `%s`, found `%s`", k.line, w, k.s.c_str());
+    };
+    kw("loop");
+    take(T_LBRACE, "'{'");
+    take(T_LPAREN, "'('");
+    f.cond_lhs = expr();
+    take(T_LT, "'<' (only counted loops are lifted)");
+    f.cond_rhs = expr();
+    take(T_RPAREN, "')'");
+    take(T_ARROW, "'->'");
+    take(T_LBRACE, "'{'");
+    take(T_MINUS, "'-true->'");
+    kw("true");
+    take(T_ARROW, "'->'");
+    take(T_LBRACE, "'{'");
+    bool cont = false;
+    while (!at(T_RBRACE)) {
+      if (at(T_ARROW)) {  // -> loop;
+        ++p;
+        kw("loop");
+        take(T_SEMI, "';'");
+        cont = true;
+        continue;
+      }
+      if (cont) unsupported("line %d: statements after `-> loop`", cur().line);
+      LoopStmt st;
+      const size_t save = p;
+      EP e = expr();
+      if (at(T_LARROW)) {
+        if (e->k != Expr::INDEX) unsupported("line %d: `<-` needs an element target", cur().line);
+        ++p;
+        st.k = LoopStmt::UPDATE;
+        st.target = e;
+        st.value = expr();
+      } else {
+        p = save;
+        st.k = LoopStmt::BIND;
+        st.chain = chain();
+      }
+      take(T_SEMI, "';'");
+      f.body.push_back(st);
+    }
+    take(T_RBRACE, "'}'");
+    if (!cont) unsupported("line %d: the loop's true branch must end with `-> loop`", f.line);
+    take(T_MINUS, "'-false->'");
+    kw("false");
+    take(T_ARROW, "'->'");
+    f.ret = expr();
+    take(T_ARROW, "'->'");
+    kw("ret");
+    take(T_SEMI, "';'");
+    take(T_RBRACE, "'}'");
+    take(T_RBRACE, "'}'");
+    take(T_RBRACE, "'}'");
+    return f;
+  }
+
   std::vector<Chain> main_body() {
     bool found = false;
     std::vector<Chain> body;
@@ -390,7 +524,11 @@ struct Parser {
       Token kw = take(T_IDENT, "'fn'");
       if (kw.s != "fn") unsupported("line %d: only `fn` items are in the subset", kw.line);
       std::string name = take(T_IDENT, "function name").s;
-      if (name != "main") unsupported("line %d: functions other than main (`%s`)", kw.line, name.c_str());
+      if (name != "main") {
+        if (fns.count(name)) unsupported("line %d: `%s` defined twice", kw.line, name.c_str());
+        fns[name] = loop_fn(name, kw.line);
+        continue;
+      }
       take(T_LPAREN, "'('");
       take(T_RPAREN, "')'");
       take(T_LBRACE, "'{'");
@@ -404,6 +542,7 @@ struct Parser {
     if (!found) unsupported("no fn main");
     return body;
   }
+
 };
 
 // ---- values ------------------------------------------------------------------------------
@@ -434,6 +573,8 @@ struct Value {
 // ---- the runner ---------------------------------------------------------------------------
 
 struct Runner {
+  const std::map<std::string, FnDef>* fns = nullptr;  // the program's counted-loop helpers
+  int synth = 0;                                       // counter for synthetic names
   bool plan = false;
   bool fast_fold = false;  // the reordered f64 tree instead of the interpreter's order
   MapalGpuCtx* ctx = nullptr;
@@ -686,6 +827,7 @@ struct Runner {
       sync_point();
       return num_f64(mapal_time_ms());
     }
+    if (fns && fns->count(n)) return call_fn(fns->at(n), v, line);
     // otherwise: a binding
     if (n == "map" || n == "fold") unsupported("line %d: %s without a body", line, n.c_str());
     (void)c;
@@ -1040,6 +1182,165 @@ struct Runner {
     return true;
   }
 
+  // -- counted-loop helpers, lifted into the cap form ---------------------------------
+  //
+  // The reference rewrites canonical counted loops into a captured Fold or
+  // Map before any backend sees them (crates/mapal-rewrite/src/lift.rs:1-12,
+  // R-LF / R-LM): `(counter, acc)` loops with counter 0..K and a pure
+  // accumulator become `(seed, K -> iota) -> fold`, and `(counter, out)` loops
+  // whose one update is `out[counter] <- value` with len(out) == K become
+  // `K -> iota -> map`. A call of a Map-form helper runs as that map site, with
+  // Fold-form helpers it calls inlined as the cell's fold: the matmul loop form
+  // (examples/matmul4_loop.mapal, benches/matmul/matmul16.mapal) becomes the
+  // matmul tile site.
+
+  static EP subst(const EP& e, const std::map<std::string, EP>& m) {
+    if (e->k == Expr::NAME) {
+      auto it = m.find(e->s);
+      return it == m.end() ? e : it->second;
+    }
+    auto c = std::make_shared<Expr>(*e);
+    for (auto& k : c->kids) k = subst(k, m);
+    return c;
+  }
+
+  static bool is_name(const EP& e, const std::string& n) { return e->k == Expr::NAME && e->s == n; }
+  static bool is_int(const EP& e, long long v) { return e->k == Expr::INT && e->ival == v; }
+
+  // `ctr + 1 -> ctr`
+  static bool is_step(const LoopStmt& st, const std::string& ctr) {
+    if (st.k != LoopStmt::BIND || st.chain.stages.size() != 1 || st.chain.stages[0].k != Stage::NAMED ||
+        st.chain.stages[0].name != ctr)
+      return false;
+    const EP& h = st.chain.head;
+    return h->k == Expr::BIN && h->op == '+' && is_name(h->kids[0], ctr) && is_int(h->kids[1], 1);
+  }
+
+  // The loop's counter: `mut ctr: i32 <- 0` compared against an integer literal K.
+  static bool counter(const FnDef& f, std::string& ctr, long long& K) {
+    if (f.cond_lhs->k != Expr::NAME || f.cond_rhs->k != Expr::INT || f.cond_rhs->ival < 1) return false;
+    ctr = f.cond_lhs->s;
+    K = f.cond_rhs->ival;
+    for (auto& m : f.muts)
+      if (m.name == ctr) return m.arr_len < 0 && is_int(m.init, 0);
+    return false;
+  }
+
+  struct FoldForm {
+    std::string ctr, acc;
+    long long K;
+    EP seed, body;
+  };
+
+  static bool fold_form(const FnDef& f, FoldForm& ff) {
+    if (f.muts.size() != 2 || !counter(f, ff.ctr, ff.K) || f.body.size() != 2) return false;
+    const FnDef::Mut& m = f.muts[0].name == ff.ctr ? f.muts[1] : f.muts[0];
+    if (m.arr_len >= 0 || !is_name(f.ret, m.name)) return false;
+    ff.acc = m.name;
+    ff.seed = m.init;
+    const LoopStmt& upd = f.body[0];
+    if (upd.k != LoopStmt::BIND || upd.chain.stages.size() != 1 || upd.chain.stages[0].k != Stage::NAMED ||
+        upd.chain.stages[0].name != ff.acc || !is_step(f.body[1], ff.ctr))
+      return false;
+    ff.body = upd.chain.head;
+    return true;
+  }
+
+  // `(seed', iota K) -> fold { acc, ctr -> body' }` for a call of a Fold-form helper
+  Chain inline_fold(const FnDef& g, const EP& args, int line) {
+    FoldForm ff;
+    if (!fold_form(g, ff)) unsupported("line %d: `%s` is not a counted fold loop", line, g.name.c_str());
+    std::map<std::string, EP> m;
+    std::vector<EP> av = args->k == Expr::TUPLE ? args->kids : std::vector<EP>{args};
+    if (av.size() != g.params.size()) unsupported("line %d: `%s` takes %zu arguments", line, g.name.c_str(), g.params.size());
+    for (size_t i = 0; i < av.size(); ++i) m[g.params[i]] = av[i];
+    if (m.count(ff.acc) || m.count(ff.ctr)) unsupported("line %d: loop variable shadows a parameter", line);
+    const std::string iota_name = "__iota" + std::to_string(synth++);
+    Value iv;
+    iv.ty = TY_IOTA;
+    iv.n = (uint64_t)ff.K;
+    env[iota_name] = iv;
+    Chain c;
+    c.line = line;
+    c.head = std::make_shared<Expr>();
+    c.head->k = Expr::TUPLE;
+    auto nm = std::make_shared<Expr>();
+    nm->k = Expr::NAME;
+    nm->s = iota_name;
+    c.head->kids = {subst(ff.seed, m), nm};
+    Stage st;
+    st.k = Stage::FOLD;
+    st.lam = std::make_shared<Lambda>();
+    st.lam->params = {ff.acc, ff.ctr};
+    Chain b;
+    b.line = line;
+    b.head = subst(ff.body, m);
+    st.lam->stmts.push_back(b);
+    c.stages.push_back(st);
+    return c;
+  }
+
+  Value call_fn(const FnDef& f, const Value& args, int line) {
+    // arguments become synthetic bindings the lifted body refers to
+    std::vector<Value> av = args.ty == TY_TUPLE ? args.items : std::vector<Value>{args};
+    if (av.size() != f.params.size())
+      unsupported("line %d: `%s` takes %zu arguments", line, f.name.c_str(), f.params.size());
+    std::map<std::string, EP> m;
+    for (size_t i = 0; i < av.size(); ++i) {
+      const std::string nm = "__arg" + std::to_string(synth++);
+      env[nm] = av[i];
+      auto e = std::make_shared<Expr>();
+      e->k = Expr::NAME;
+      e->s = nm;
+      m[f.params[i]] = e;
+    }
+    std::string ctr;
+    long long K = 0;
+    if (f.muts.size() != 2 || !counter(f, ctr, K) || f.body.size() < 2 || !is_step(f.body.back(), ctr))
+      unsupported("line %d: `%s` is not a counted map loop", line, f.name.c_str());
+    const FnDef::Mut& out = f.muts[0].name == ctr ? f.muts[1] : f.muts[0];
+    const LoopStmt& upd = f.body[f.body.size() - 2];
+    if (out.arr_len != K || !is_name(f.ret, out.name) || upd.k != LoopStmt::UPDATE ||
+        !is_name(upd.target->kids[0], out.name) || !is_name(upd.target->kids[1], ctr))
+      unsupported("line %d: `%s` must write every element out[%s] of a length-%lld array", line, f.name.c_str(),
+                  ctr.c_str(), K);
+    if (m.count(ctr)) unsupported("line %d: loop variable shadows a parameter", line);
+    auto L = std::make_shared<Lambda>();
+    L->params = {ctr};
+    std::string call_result;
+    Chain call_chain;
+    for (size_t i = 0; i + 2 < f.body.size(); ++i) {
+      const LoopStmt& st = f.body[i];
+      if (st.k != LoopStmt::BIND) unsupported("line %d: only out[%s] may be updated", line, ctr.c_str());
+      const Chain& c = st.chain;
+      if (c.stages.size() == 2 && c.stages[0].k == Stage::NAMED && fns->count(c.stages[0].name) &&
+          c.stages[1].k == Stage::NAMED) {
+        if (!call_result.empty()) unsupported("line %d: more than one helper call in a map loop", line);
+        call_result = c.stages[1].name;
+        call_chain = inline_fold(fns->at(c.stages[0].name), subst(c.head, m), line);
+        continue;
+      }
+      if (c.stages.size() != 1 || c.stages[0].k != Stage::NAMED) unsupported("line %d: map loop statement", line);
+      Chain b = c;
+      b.head = subst(c.head, m);
+      L->stmts.push_back(b);
+    }
+    if (!call_result.empty()) {
+      if (!is_name(upd.value, call_result)) unsupported("line %d: the helper's result must be the stored value", line);
+      L->stmts.push_back(call_chain);
+    } else {
+      Chain b;
+      b.line = line;
+      b.head = subst(upd.value, m);
+      L->stmts.push_back(b);
+    }
+    Value dom;
+    dom.ty = TY_IOTA;
+    dom.n = (uint64_t)K;
+    say("lift " + f.name + ": counted loop over " + std::to_string(K) + " -> map");
+    return map_site(*L, dom, line);
+  }
+
   // -- the general map body -> MAPAL_X_* program --
 
   struct Compiler {
@@ -1210,6 +1511,7 @@ int main(int argc, char** argv) {
   Parser P{lex(src)};
   std::vector<Chain> body = P.main_body();
   Runner R;
+  R.fns = &P.fns;
   R.plan = plan;
   R.fast_fold = fast_fold;
   mapal_time_ms();  // start the process clock, as the reference's runtime does on first use

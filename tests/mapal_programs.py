@@ -115,3 +115,58 @@ FLOAT_PRINT = """fn main() {
     -7.5 % 2.0 -> println;
 }
 """
+
+
+def matmul_loops(n: int, literals: bool = False) -> str:
+    """The same product in the counted-loop form: a dot-product helper with a
+    (counter, accumulator) loop and a product helper whose loop writes every
+    element of its result once, which the driver lifts into fold / map."""
+    nn = n * n
+    if literals:
+        gen = lambda mul, add: ", ".join(f"{((t * mul + add) % 101) - 50}.0" for t in range(nn))
+        inputs = f"""    [{gen(7, 13)}] -> a;
+    [{gen(7, 57)}] -> b;"""
+    else:
+        inputs = f"""    {nn} -> iota -> cells;
+    cells -> map {{ t -> {GEN_A} }} -> a;
+    cells -> map {{ t -> {GEN_B} }} -> b;"""
+    return f"""fn dot(x: [f32; {nn}], y: [f32; {nn}], row: i32, col: i32) -> f32 {{
+    mut s: i32 <- 0;
+    mut total: f32 <- 0.0;
+    loop {{
+        (s < {n}) -> {{
+            -true-> {{
+                total + x[row * {n} + s] * y[s * {n} + col] -> total;
+                s + 1 -> s;
+                -> loop;
+            }}
+            -false-> total -> ret;
+        }}
+    }}
+}}
+
+fn product(x: [f32; {nn}], y: [f32; {nn}]) -> [f32; {nn}] {{
+    mut out: [f32; {nn}] <- x;
+    mut cell: i32 <- 0;
+    loop {{
+        (cell < {nn}) -> {{
+            -true-> {{
+                cell / {n} -> r;
+                cell % {n} -> c;
+                (x, y, r, c) -> dot -> v;
+                out[cell] <- v;
+                cell + 1 -> cell;
+                -> loop;
+            }}
+            -false-> out -> ret;
+        }}
+    }}
+}}
+
+fn main() {{
+{inputs}
+    (a, b) -> product -> prod;
+    prod[0] -> println;
+    prod[{nn - 1}] -> println;
+}}
+"""

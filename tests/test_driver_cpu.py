@@ -123,8 +123,22 @@ def test_plan_general_body_uses_map_expr(tmp_path):
     assert "map_expr n=100 ops=8 arrays=1" in r.stdout
 
 
+def test_plan_lifts_counted_loops(tmp_path):
+    # the loop form of the product becomes the matmul tile site (lift.rs R-LF / R-LM)
+    for prog in (P.matmul_loops(16), P.matmul_loops(4, literals=True)):
+        r = _plan(prog, tmp_path)
+        assert r.returncode == 0, r.stderr
+        n = 16 if "16 -> iota" in prog or "[f32; 256]" in prog else 4
+        assert f"lift product: counted loop over {n * n} -> map" in r.stdout
+        assert (f"tile_site rows={n} c={n} k={n} a{{base=0 ci={n} ck=1 clane=0 ks=0/0/0}} "
+                f"b{{base=0 ci=0 ck={n} clane=1 ks=0/0/0}}") in r.stdout.split("\n")
+
+
 @pytest.mark.parametrize("src,why", [
-    ("fn helper() { 1 -> println; }\nfn main() { 1 -> println; }\n", "functions other than main"),
+    ("fn helper() { 1 -> println; }\nfn main() { 1 -> println; }\n", "expected"),
+    ("fn f(x: i32) -> i32 {\n mut k: i32 <- 0;\n mut s: i32 <- 0;\n loop {\n (k < 4) -> {\n -true-> {\n"
+     " s + x -> s;\n k + 2 -> k;\n -> loop;\n }\n -false-> s -> ret;\n }\n }\n}\n"
+     "fn main() {\n 4 -> iota -> d;\n d -> f -> e;\n}\n", "counted map loop"),
     ("fn main() {\n mut k: i32 <- 0;\n}\n", "expected"),
     ("fn main() {\n 10 -> iota -> d;\n d -> map { i -> i -> widen_f64 } -> e;\n}\n", "map body stage"),
     ("fn main() {\n 10 -> iota -> d;\n d -> map { i -> (1, d) -> fold { a, v -> a * v } } -> e;\n}\n",

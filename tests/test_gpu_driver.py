@@ -55,3 +55,17 @@ def test_matmul_4096_known_answer(tmp_path):
     r = _run(str(f))
     assert r.returncode == 0, r.stderr
     assert r.stdout == "74348\n-302529\n"
+
+
+@pytest.mark.parametrize("n,literals", [(4, True), (16, False), (64, False), (256, False)])
+def test_loop_form_matmul_known_answers(n, literals, tmp_path):
+    # the counted-loop form, lifted to the tile site, prints the reference's
+    # published answers for the same inputs
+    import json
+    gold = json.load(open(os.path.join(HERE, "golden", "reference_outputs.json")))["matmul_known_answers"]
+    case = [c for c in gold if c["n"] == n][0]
+    f = tmp_path / f"matmul_loops_{n}.mapal"
+    f.write_text(P.matmul_loops(n, literals))
+    r = _run(str(f))
+    assert r.returncode == 0, r.stderr
+    assert r.stdout == f"{case['c0']}\n{case['clast']}\n"

@@ -17,6 +17,8 @@
 //   (x, y) -> zip -> map { p -> ... }  zipped inputs
 //   (seed, xs) -> fold { acc, v -> acc + v }   the sum fold
 //   a[i] -> println, "text" -> print, () -> time, scalar arithmetic
+//   (x, y) -> helper -> z              a counted-loop helper, lifted into a
+//                                      map (and the fold helpers it calls)
 //
 // Scalars live on the host; arrays live on the device. Printing goes through
 // mapal_print_* (Rust Display text, as mapal-rt/src/lib.rs:27-60), traps

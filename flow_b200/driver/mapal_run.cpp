@@ -1,6 +1,6 @@
 // mapal_run.cpp — run a Mapal program's `main` with every bulk site on the GPU.
 //
-//   mapal-run [--device D] [--plan] [--fast-fold] program.mapal
+//   mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] program.mapal
 //
 // The reference compiles a program to CUDA C++ (`emit`, crates/backends/cuda/
 // src/lib.rs:72-111) and the emitted `main` launches one generated kernel per
@@ -28,8 +28,11 @@
 // GPU (arrays are then shapes only). Top-level f32 sum folds run in the
 // interpreter's order (bit-exact stdout); --fast-fold takes the bandwidth-bound
 // reordered tree instead, whose result is within its stated tolerance.
+// --gpus N partitions matmul sites across N devices (row blocks, B broadcast);
+// every other site runs on the first device.
 #include <cuda_runtime.h>
 #include <stdarg.h>
+#include <unistd.h>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -71,6 +74,25 @@ void check(int rc, const char* what) {
   if (rc == MAPAL_TRAP_INDEX_OOB) mapal_trap(1);
   infra(std::string(what) + ": " + mapal_gpu_last_error());
 }
+
+// While alive, anything written to stdout goes to stderr: NCCL prints its
+// version banner on stdout at communicator set-up, and the program's stdout
+// must hold exactly what the program prints.
+struct StdoutToStderr {
+  int saved;
+  StdoutToStderr() {
+    fflush(stdout);
+    saved = dup(1);
+    dup2(2, 1);
+  }
+  ~StdoutToStderr() {
+    fflush(stdout);
+    if (saved >= 0) {
+      dup2(saved, 1);
+      close(saved);
+    }
+  }
+};
 
 // ---- lexer -----------------------------------------------------------------------------
 
@@ -576,6 +598,8 @@ struct Value {
 
 struct Runner {
   const std::map<std::string, FnDef>* fns = nullptr;  // the program's counted-loop helpers
+  int gpus = 1;   // devices dev0 .. dev0 + gpus - 1; matmul sites are partitioned across them
+  int dev0 = 0;
   int synth = 0;                                       // counter for synthetic names
   bool plan = false;
   bool fast_fold = false;  // the reordered f64 tree instead of the interpreter's order
@@ -1125,11 +1149,82 @@ struct Runner {
              (unsigned long long)s.b.ck, (unsigned long long)s.b.clane, (unsigned long long)s.b.ksplit.div,
              (unsigned long long)s.b.ksplit.cq, (unsigned long long)s.b.ksplit.cr);
     say(desc);
+    if (gpus > 1 && matmul_shaped(s) && s.rows >= (uint64_t)gpus) return matmul_partitioned(s, A, B);
     Value out = make_array(TY_F32, n);
     if (!plan)
       check(mapal_gpu_tile_site_f32(ctx, &s, (const float*)A.ptr(), (const float*)B.ptr(), (float*)out.ptr(),
                                     MAPAL_MATMUL_STRICT),
             "tile_site");
+    return out;
+  }
+
+  static bool matmul_shaped(const MapalTileSite& s) {
+    return s.k > 0 && s.a.ksplit.div == 0 && s.b.ksplit.div == 0 && s.a.ck == 1 && s.a.clane == 0 &&
+           s.b.ci == 0 && s.b.clane == 1 && s.a.ci >= s.k && s.b.ck >= s.c;
+  }
+
+  // The partitioner's matmul rule (row blocks of A and C per device, B
+  // replicated by the sharded entry point's NCCL broadcast): arrays live on
+  // the first device, so each other device receives its A rows by a peer copy
+  // and returns its C rows the same way. Strict results are bit-identical to
+  // the one-device site: no cell's k order changes.
+  Value matmul_partitioned(const MapalTileSite& s, const Value& A, const Value& B) {
+    std::vector<uint64_t> lo(gpus), hi(gpus), m(gpus);
+    std::string rows;
+    for (int d = 0; d < gpus; ++d) {
+      mapal_gpu_shard_range(s.rows, gpus, d, &lo[d], &hi[d]);
+      m[d] = hi[d] - lo[d];
+      rows += (d ? "," : "") + std::to_string(m[d]);
+    }
+    say("matmul_f32_sharded gpus=" + std::to_string(gpus) + " rows=" + rows);
+    // the Index rule before any copy: a read outside an operand traps
+    const unsigned __int128 a_max = (unsigned __int128)s.a.base + (unsigned __int128)(s.rows - 1) * s.a.ci + (s.k - 1);
+    const unsigned __int128 b_max = (unsigned __int128)s.b.base + (unsigned __int128)(s.k - 1) * s.b.ck + (s.c - 1);
+    if (a_max >= A.n || b_max >= B.n) mapal_trap(1);
+    Value out = make_array(TY_F32, s.rows * s.c);
+    if (plan) return out;
+    sync_point();  // A and B are final on the first device
+    const uint64_t lda = s.a.ci, K = s.k, N = s.c;
+    const float* abase = (const float*)A.ptr() + s.a.base;
+    std::vector<const float*> ap(gpus);
+    std::vector<float*> bp(gpus), cp(gpus);
+    auto cuda = [](cudaError_t e, const char* what) {
+      if (e != cudaSuccess) infra(std::string(what) + ": " + cudaGetErrorString(e));
+    };
+    for (int d = 0; d < gpus; ++d) {
+      if (d == 0) {
+        ap[0] = abase + lo[0] * lda;
+        bp[0] = (float*)B.ptr();
+        cp[0] = (float*)out.ptr() + lo[0] * N;
+        continue;
+      }
+      const uint64_t a_elems = m[d] ? (m[d] - 1) * lda + K : 0;
+      float *a_d = nullptr, *b_d = nullptr, *c_d = nullptr;
+      cuda(cudaSetDevice(dev0 + d), "cudaSetDevice");
+      cuda(cudaMalloc(&a_d, (a_elems ? a_elems : 1) * 4), "cudaMalloc");
+      cuda(cudaMalloc(&b_d, (s.b.len ? s.b.len : 1) * 4), "cudaMalloc");
+      cuda(cudaMalloc(&c_d, (m[d] * N ? m[d] * N : 1) * 4), "cudaMalloc");
+      if (a_elems) cuda(cudaMemcpyPeer(a_d, dev0 + d, abase + lo[d] * lda, dev0, a_elems * 4), "cudaMemcpyPeer");
+      ap[d] = a_d;
+      bp[d] = b_d;
+      cp[d] = c_d;
+    }
+    cuda(cudaSetDevice(dev0), "cudaSetDevice");
+    {
+      StdoutToStderr quiet;
+      check(mapal_gpu_matmul_f32_sharded(ctx, &s, ap.data(), bp.data(), cp.data(), m.data(), 0,
+                                         MAPAL_MATMUL_STRICT),
+            "matmul_f32_sharded");
+      check(mapal_gpu_synchronize(ctx), "synchronize");
+    }
+    for (int d = 1; d < gpus; ++d) {
+      if (m[d]) cuda(cudaMemcpyPeer(cp[0] - lo[0] * N + lo[d] * N, dev0, cp[d], dev0 + d, m[d] * N * 4), "cudaMemcpyPeer");
+      cuda(cudaSetDevice(dev0 + d), "cudaSetDevice");
+      cudaFree((void*)ap[d]);
+      cudaFree(bp[d]);
+      cudaFree(cp[d]);
+    }
+    cuda(cudaSetDevice(dev0), "cudaSetDevice");
     return out;
   }
 
@@ -1487,16 +1582,21 @@ struct Runner {
 
 int main(int argc, char** argv) {
   bool plan = false, fast_fold = false;
-  int device = 0;
+  int device = 0, gpus = 1;
   const char* path = nullptr;
   for (int a = 1; a < argc; ++a) {
     if (!strcmp(argv[a], "--plan")) plan = true;
     else if (!strcmp(argv[a], "--fast-fold")) fast_fold = true;
     else if (!strcmp(argv[a], "--device") && a + 1 < argc) device = atoi(argv[++a]);
+    else if (!strcmp(argv[a], "--gpus") && a + 1 < argc) gpus = atoi(argv[++a]);
     else path = argv[a];
   }
   if (!path) {
-    fprintf(stderr, "usage: mapal-run [--device D] [--plan] [--fast-fold] program.mapal\n");
+    fprintf(stderr, "usage: mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] program.mapal\n");
+    return 2;
+  }
+  if (gpus < 1 || device < 0 || device + gpus > 32) {
+    fprintf(stderr, "mapal-run: bad --device / --gpus\n");
     return 2;
   }
   FILE* f = fopen(path, "rb");
@@ -1514,12 +1614,20 @@ int main(int argc, char** argv) {
   std::vector<Chain> body = P.main_body();
   Runner R;
   R.fns = &P.fns;
+  R.gpus = gpus;
+  R.dev0 = device;
   R.plan = plan;
   R.fast_fold = fast_fold;
   mapal_time_ms();  // start the process clock, as the reference's runtime does on first use
   if (!plan) {
+    int have = 0;
+    check(mapal_gpu_device_count(&have), "device_count");
+    if (device + gpus > have) infra("fewer devices than --device + --gpus");
     if (cudaSetDevice(device) != cudaSuccess) infra("cudaSetDevice");
-    check(mapal_gpu_ctx_create(1u << device, &R.ctx), "ctx_create");
+    {
+      StdoutToStderr quiet;  // a multi-device context sets up NCCL communicators
+      check(mapal_gpu_ctx_create(((1u << gpus) - 1) << device, &R.ctx), "ctx_create");
+    }
     // the legacy default stream orders the sites with this driver's own copies
     check(mapal_gpu_set_stream(R.ctx, 0, nullptr), "set_stream");
     check(mapal_gpu_set_sync(R.ctx, 0), "set_sync");

@@ -148,3 +148,13 @@ def test_plan_refuses_outside_subset(src, why, tmp_path):
     r = _plan(src, tmp_path)
     assert r.returncode == 2
     assert "unsupported" in r.stderr and why in r.stderr
+
+
+def test_plan_partitions_matmul_across_gpus(tmp_path):
+    f = tmp_path / "mm.mapal"
+    f.write_text(P.matmul(64))
+    r = subprocess.run([DRIVER, "--plan", "--gpus", "3", str(f)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    assert "matmul_f32_sharded gpus=3 rows=22,21,21" in r.stdout
+    # every other site stays on the first device
+    assert "gen_affine n=4096 mul=7 add=13 mod=101 sub=50" in r.stdout

@@ -69,3 +69,20 @@ def test_loop_form_matmul_known_answers(n, literals, tmp_path):
     r = _run(str(f))
     assert r.returncode == 0, r.stderr
     assert r.stdout == f"{case['c0']}\n{case['clast']}\n"
+
+
+@pytest.mark.parametrize("name,src", [("matmul_256", P.matmul(256)), ("matmul_frac_96", None),
+                                      ("loops_64", P.matmul_loops(64))])
+def test_matmul_partitioned_across_gpus(name, src, tmp_path):
+    # --gpus 2: row blocks of A and C per device, B broadcast; the same bytes
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    if src is None:
+        src = open(os.path.join(HERE, "programs", "matmul_frac_96.mapal")).read()
+    f = tmp_path / f"{name}.mapal"
+    f.write_text(src)
+    one = subprocess.run([DRIVER, str(f)], capture_output=True, text=True, timeout=300)
+    two = subprocess.run([DRIVER, "--gpus", "2", str(f)], capture_output=True, text=True, timeout=300)
+    assert one.returncode == 0 and two.returncode == 0, (one.stderr, two.stderr)
+    assert two.stdout == one.stdout

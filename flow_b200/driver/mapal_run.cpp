@@ -1,6 +1,6 @@
 // mapal_run.cpp — run a Mapal program's `main` with every bulk site on the GPU.
 //
-//   mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] program.mapal
+//   mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] [--tf32x3] program.mapal
 //
 // The reference compiles a program to CUDA C++ (`emit`, crates/backends/cuda/
 // src/lib.rs:72-111) and the emitted `main` launches one generated kernel per
@@ -29,7 +29,9 @@
 // interpreter's order (bit-exact stdout); --fast-fold takes the bandwidth-bound
 // reordered tree instead, whose result is within its stated tolerance.
 // --gpus N partitions matmul sites across N devices (row blocks, B broadcast);
-// every other site runs on the first device.
+// every other site runs on the first device. --tf32x3 runs matmul-shaped
+// sites on the tensor cores (3xTF32, within its stated tolerance) for programs
+// whose precision contract allows it; the default stays strict.
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <unistd.h>
@@ -599,6 +601,7 @@ struct Value {
 struct Runner {
   const std::map<std::string, FnDef>* fns = nullptr;  // the program's counted-loop helpers
   int gpus = 1;   // devices dev0 .. dev0 + gpus - 1; matmul sites are partitioned across them
+  int mm_mode = MAPAL_MATMUL_STRICT;  // --tf32x3: matmul-shaped sites on the tensor cores
   int dev0 = 0;
   int synth = 0;                                       // counter for synthetic names
   bool plan = false;
@@ -1149,11 +1152,12 @@ struct Runner {
              (unsigned long long)s.b.ck, (unsigned long long)s.b.clane, (unsigned long long)s.b.ksplit.div,
              (unsigned long long)s.b.ksplit.cq, (unsigned long long)s.b.ksplit.cr);
     say(desc);
+    if (mm_mode == MAPAL_MATMUL_TF32X3 && matmul_shaped(s)) say("matmul mode tf32x3");
     if (gpus > 1 && matmul_shaped(s) && s.rows >= (uint64_t)gpus) return matmul_partitioned(s, A, B);
     Value out = make_array(TY_F32, n);
     if (!plan)
       check(mapal_gpu_tile_site_f32(ctx, &s, (const float*)A.ptr(), (const float*)B.ptr(), (float*)out.ptr(),
-                                    MAPAL_MATMUL_STRICT),
+                                    mm_mode),
             "tile_site");
     return out;
   }
@@ -1212,8 +1216,7 @@ struct Runner {
     cuda(cudaSetDevice(dev0), "cudaSetDevice");
     {
       StdoutToStderr quiet;
-      check(mapal_gpu_matmul_f32_sharded(ctx, &s, ap.data(), bp.data(), cp.data(), m.data(), 0,
-                                         MAPAL_MATMUL_STRICT),
+      check(mapal_gpu_matmul_f32_sharded(ctx, &s, ap.data(), bp.data(), cp.data(), m.data(), 0, mm_mode),
             "matmul_f32_sharded");
       check(mapal_gpu_synchronize(ctx), "synchronize");
     }
@@ -1581,18 +1584,19 @@ struct Runner {
 }  // namespace
 
 int main(int argc, char** argv) {
-  bool plan = false, fast_fold = false;
+  bool plan = false, fast_fold = false, tf32x3 = false;
   int device = 0, gpus = 1;
   const char* path = nullptr;
   for (int a = 1; a < argc; ++a) {
     if (!strcmp(argv[a], "--plan")) plan = true;
     else if (!strcmp(argv[a], "--fast-fold")) fast_fold = true;
+    else if (!strcmp(argv[a], "--tf32x3")) tf32x3 = true;
     else if (!strcmp(argv[a], "--device") && a + 1 < argc) device = atoi(argv[++a]);
     else if (!strcmp(argv[a], "--gpus") && a + 1 < argc) gpus = atoi(argv[++a]);
     else path = argv[a];
   }
   if (!path) {
-    fprintf(stderr, "usage: mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] program.mapal\n");
+    fprintf(stderr, "usage: mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] [--tf32x3] program.mapal\n");
     return 2;
   }
   if (gpus < 1 || device < 0 || device + gpus > 32) {
@@ -1615,6 +1619,7 @@ int main(int argc, char** argv) {
   Runner R;
   R.fns = &P.fns;
   R.gpus = gpus;
+  R.mm_mode = tf32x3 ? MAPAL_MATMUL_TF32X3 : MAPAL_MATMUL_STRICT;
   R.dev0 = device;
   R.plan = plan;
   R.fast_fold = fast_fold;

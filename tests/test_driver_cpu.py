@@ -158,3 +158,10 @@ def test_plan_partitions_matmul_across_gpus(tmp_path):
     assert "matmul_f32_sharded gpus=3 rows=22,21,21" in r.stdout
     # every other site stays on the first device
     assert "gen_affine n=4096 mul=7 add=13 mod=101 sub=50" in r.stdout
+
+
+def test_plan_tf32x3_mode(tmp_path):
+    f = tmp_path / "mm.mapal"
+    f.write_text(P.matmul(32))
+    r = subprocess.run([DRIVER, "--plan", "--tf32x3", str(f)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and "matmul mode tf32x3" in r.stdout

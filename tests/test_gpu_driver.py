@@ -86,3 +86,13 @@ def test_matmul_partitioned_across_gpus(name, src, tmp_path):
     two = subprocess.run([DRIVER, "--gpus", "2", str(f)], capture_output=True, text=True, timeout=300)
     assert one.returncode == 0 and two.returncode == 0, (one.stderr, two.stderr)
     assert two.stdout == one.stdout
+
+
+def test_tf32x3_mode_on_integer_inputs(tmp_path):
+    # the benches' integer generators give products and sums exact in the
+    # 3xTF32 split, so the tensor-core mode prints the same known answers
+    f = tmp_path / "matmul_256.mapal"
+    f.write_text(P.matmul(256))
+    r = subprocess.run([DRIVER, "--tf32x3", str(f)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout == "-3694\n10946\n"

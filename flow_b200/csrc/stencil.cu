@@ -46,10 +46,14 @@ __host__ __device__ constexpr int fir_wpad(int taps) { return (taps + 3) & ~3; }
 __host__ __device__ constexpr int fir_npairs(int taps) { return kFirHalf + fir_wpad(taps) + 8; }
 
 // y[t] = fold_k(acc + w[k] * x[t + k]) from seed, t in [0, n_out).
-__global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restrict__ w, int taps,
+// TAPS > 0: the tap count is a compile-time constant and the tap loop fully
+// unrolls (no register moves to slide the window; 64 taps: +7-9 % on B200).
+template <int TAPS>
+__global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restrict__ w, int taps_rt,
                                                           const float* __restrict__ x, uint64_t x_len,
                                                           float* __restrict__ y, uint64_t n_out,
                                                           float seed, float neg_zero) {
+  const int taps = TAPS ? TAPS : taps_rt;
   extern __shared__ __align__(16) float fir_smem[];
   const int wpad = fir_wpad(taps), npairs = fir_npairs(taps);
   float* wp = fir_smem;                   // [wpad + 4] splat pairs (w[k], w[k]), zero past the taps
@@ -91,6 +95,7 @@ __global__ void __launch_bounds__(kFirThreads) fir_kernel(const float* __restric
   }
   // loads for the next tap group are issued one group ahead
   ulonglong2 pe = ev[1], po = ov[1], pw0 = wv[0], pw1 = wv[1];
+#pragma unroll
   for (int kg = 0; kg < taps; kg += 4) {
     win[4] = pe.x, win[5] = pe.y, win[6] = po.x, win[7] = po.y;
     const f2 wk[4] = {pw0.x, pw0.y, pw1.x, pw1.y};
@@ -223,19 +228,30 @@ static size_t fir_smem_bytes(uint64_t taps) {
   return sizeof(float) * 2 * ((size_t)fir_wpad((int)taps) + 4 + (size_t)fir_npairs((int)taps));
 }
 
+template <int TAPS>
+int launch_fir_t(cudaStream_t s, size_t smem, const float* w, uint64_t taps, const float* x, uint64_t x_len,
+                 float* y, uint64_t n_out, float seed) {
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(fir_kernel<TAPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fir)");
+  }
+  const uint64_t blocks = (n_out + kFirTile - 1) / kFirTile;
+  if (blocks > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
+  fir_kernel<TAPS><<<(unsigned)blocks, kFirThreads, smem, s>>>(w, (int)taps, x, x_len, y, n_out, seed, -0.0f);
+  count_launch();
+  return 0;
+}
+
 int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, uint64_t x_len, float* y,
                uint64_t n_out, float seed) {
   size_t smem = fir_smem_bytes(taps);
   if (smem == 0) return MAPAL_ERR_UNSUPPORTED;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(fir_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(fir)");
+  switch (taps) {  // the benches' tap counts get an unrolled kernel
+    case 16: return launch_fir_t<16>(s, smem, w, taps, x, x_len, y, n_out, seed);
+    case 32: return launch_fir_t<32>(s, smem, w, taps, x, x_len, y, n_out, seed);
+    case 64: return launch_fir_t<64>(s, smem, w, taps, x, x_len, y, n_out, seed);
+    default: return launch_fir_t<0>(s, smem, w, taps, x, x_len, y, n_out, seed);
   }
-  uint64_t blocks = (n_out + kFirTile - 1) / kFirTile;
-  if (blocks > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
-  fir_kernel<<<(unsigned)blocks, kFirThreads, smem, s>>>(w, (int)taps, x, x_len, y, n_out, seed, -0.0f);
-  count_launch();
-  return 0;
 }
 
 int launch_conv3x3(cudaStream_t s, int sms, const float* w, const float* img, uint64_t img_len, uint64_t stride,

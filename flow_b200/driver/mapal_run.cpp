@@ -1141,6 +1141,12 @@ struct Runner {
     };
     fill(fa, s.a, A.n);
     fill(fbb, s.b, B.n);
+    say(describe(s));
+    if (nt_shaped(s)) return matmul_nt(s, A, B, line);
+    return run_tile(s, A, B);
+  }
+
+  static std::string describe(const MapalTileSite& s) {
     char desc[512];
     snprintf(desc, sizeof desc,
              "tile_site rows=%llu c=%llu k=%llu a{base=%llu ci=%llu ck=%llu clane=%llu ks=%llu/%llu/%llu} "
@@ -1151,15 +1157,47 @@ struct Runner {
              (unsigned long long)s.a.ksplit.cr, (unsigned long long)s.b.base, (unsigned long long)s.b.ci,
              (unsigned long long)s.b.ck, (unsigned long long)s.b.clane, (unsigned long long)s.b.ksplit.div,
              (unsigned long long)s.b.ksplit.cq, (unsigned long long)s.b.ksplit.cr);
-    say(desc);
+    return desc;
+  }
+
+  Value run_tile(const MapalTileSite& s, const Value& A, const Value& B) {
     if (mm_mode == MAPAL_MATMUL_TF32X3 && matmul_shaped(s)) say("matmul mode tf32x3");
     if (gpus > 1 && matmul_shaped(s) && s.rows >= (uint64_t)gpus) return matmul_partitioned(s, A, B);
-    Value out = make_array(TY_F32, n);
+    Value out = make_array(TY_F32, s.rows * s.c);
     if (!plan)
       check(mapal_gpu_tile_site_f32(ctx, &s, (const float*)A.ptr(), (const float*)B.ptr(), (float*)out.ptr(),
                                     mm_mode),
             "tile_site");
     return out;
+  }
+
+  // A * B^T: b reads B[base + k + lane * ldb] (B holds the right operand's
+  // columns as rows, e.g. benches/shapes/attn_256_rowmajor.mapal).
+  static bool nt_shaped(const MapalTileSite& s) {
+    return s.k > 0 && s.a.ksplit.div == 0 && s.b.ksplit.div == 0 && s.a.ck == 1 && s.a.clane == 0 &&
+           s.a.ci >= s.k && s.b.ci == 0 && s.b.ck == 1 && s.b.clane >= s.k && s.c > 1;
+  }
+
+  // Relayout first, then the plain matmul site: a move site writes the K x N
+  // operand (T[k*N + n] = B[base + n*ldb + k]), and the matmul reads it row-major.
+  // Every cell keeps its k order, so the result is the same bit for bit.
+  Value matmul_nt(const MapalTileSite& s, const Value& A, const Value& B, int line) {
+    const uint64_t K = s.k, N = s.c, ldb = s.b.clane;
+    const unsigned __int128 b_max = (unsigned __int128)s.b.base + (unsigned __int128)(N - 1) * ldb + (K - 1);
+    if (b_max >= B.n) mapal_trap(1);  // the Index rule, as the site itself would apply it
+    MapalMoveSite mv{N, K, 1, ldb, B.n - s.b.base};
+    say("move_site width=" + std::to_string(N) + " rows=" + std::to_string(K) + " cq=1 cr=" + std::to_string(ldb) +
+        " (B^T -> K x N)");
+    Value T = make_array(TY_F32, K * N);
+    if (!plan) check(mapal_gpu_transpose(ctx, &mv, (const float*)B.ptr() + s.b.base, (float*)T.ptr()), "move_site");
+    MapalTileSite m = s;
+    m.b.base = 0;
+    m.b.ck = N;
+    m.b.clane = 1;
+    m.b.len = K * N;
+    (void)line;
+    say(describe(m));
+    return run_tile(m, A, T);
   }
 
   static bool matmul_shaped(const MapalTileSite& s) {

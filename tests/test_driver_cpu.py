@@ -165,3 +165,13 @@ def test_plan_tf32x3_mode(tmp_path):
     f.write_text(P.matmul(32))
     r = subprocess.run([DRIVER, "--plan", "--tf32x3", str(f)], capture_output=True, text=True, timeout=60)
     assert r.returncode == 0 and "matmul mode tf32x3" in r.stdout
+
+
+def test_plan_nt_matmul_relayouts_then_matmul():
+    path = os.path.join(HERE, "programs", "matmul_nt_48x40x36.mapal")
+    r = subprocess.run([DRIVER, "--plan", path], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0, r.stderr
+    lines = r.stdout.split("\n")
+    assert "move_site width=40 rows=36 cq=1 cr=36 (B^T -> K x N)" in lines
+    assert ("tile_site rows=48 c=40 k=36 a{base=0 ci=36 ck=1 clane=0 ks=0/0/0} "
+            "b{base=0 ci=0 ck=40 clane=1 ks=0/0/0}") in lines

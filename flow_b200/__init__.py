@@ -256,6 +256,10 @@ class Context:
         """out (one device float) = seed + sum(x), tree order, f64 accumulation."""
         _check(lib().mapal_gpu_fold_sum_f32(self._h, seed, _ptr(x), x.numel(), _ptr(out)))
 
+    def fold_sum_i32(self, x, out, seed: int = 0) -> None:
+        """out (one device int32) = seed + sum(x) with wrapping i32 arithmetic (exact in any order)."""
+        _check(lib().mapal_gpu_fold_sum_i32(self._h, seed, _ptr(x), x.numel(), _ptr(out)))
+
     def fold_sum_strict(self, x, out, seed: float = 0.0) -> None:
         """out (one device float) = the interpreter's left fold of x from seed, bit-exact."""
         _check(lib().mapal_gpu_fold_sum_f32_strict(self._h, seed, _ptr(x), x.numel(), _ptr(out)))

@@ -52,6 +52,7 @@ SIGNATURES: dict[str, tuple] = {
     "mapal_gpu_gather": (_int, [_vp, _vp, _u64, _vp, _vp, _u64]),
     "mapal_gpu_fold_sum_f32": (_int, [_vp, _f32, _vp, _u64, _vp]),
     "mapal_gpu_fold_sum_f32_strict": (_int, [_vp, _f32, _vp, _u64, _vp]),
+    "mapal_gpu_fold_sum_i32": (_int, [_vp, _i32, _vp, _u64, _vp]),
     "mapal_gpu_fold_sum_f32_noalloc": (_int, [_f32, _vp, _u64, _vp, _vp]),
     "mapal_gpu_fir_f32": (_int, [_vp, _c.POINTER(TileSite), _vp, _vp, _vp]),
     "mapal_gpu_conv2d_3x3_f32": (_int, [_vp, _c.POINTER(TileSite), _vp, _vp, _vp]),

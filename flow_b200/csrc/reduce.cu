@@ -180,6 +180,46 @@ int launch_fold_sum_strict(cudaStream_t s, const float* x, uint64_t n, float see
   return 0;
 }
 
+namespace {
+
+// out = seed, then every block adds its wrapping partial sum atomically.
+__global__ void set_i32_kernel(int32_t* out, int32_t v) { *out = v; }
+
+__global__ void __launch_bounds__(kThreads) fold_sum_i32_kernel(const int32_t* __restrict__ x, uint64_t n,
+                                                                int32_t* out) {
+  __shared__ uint32_t part[kWarps];
+  uint32_t acc = 0;
+  for (uint64_t i = blockIdx.x * (uint64_t)kThreads + threadIdx.x; i < n; i += (uint64_t)gridDim.x * kThreads)
+    acc += (uint32_t)__ldcs(x + i);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t t = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) t += part[w];
+    atomicAdd(reinterpret_cast<unsigned*>(out), t);
+  }
+}
+
+}  // namespace
+
+extern "C" int mapal_gpu_fold_sum_i32(MapalGpuCtx* ctx, int32_t seed, const int32_t* x, uint64_t n,
+                                      int32_t* out) {
+  MAPAL_TRY(enter(ctx));
+  if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
+  if (n && !x) return set_error(MAPAL_ERR_INVALID, "x is null");
+  DeviceSlot& d = ctx->dev[0];
+  set_i32_kernel<<<1, 1, 0, d.stream>>>(out, seed);
+  count_launch();
+  if (n) {
+    fold_sum_i32_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 4), kThreads, 0, d.stream>>>(x, n, out);
+    count_launch();
+  }
+  return finish(ctx, 0, false);
+}
+
 int launch_finalize_sum(cudaStream_t s, const double* total, float seed, float* out) {
   finalize_sum_kernel<<<1, 1, 0, s>>>(total, seed, out); count_launch();
   return 0;

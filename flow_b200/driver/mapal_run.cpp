@@ -15,7 +15,8 @@
 //                                      the affine integer generator) or else
 //                                      the general map body program
 //   (x, y) -> zip -> map { p -> ... }  zipped inputs
-//   (seed, xs) -> fold { acc, v -> acc + v }   the sum fold
+//   (seed, xs) -> fold { acc, v -> acc + v }   the sum fold (f32 or i32)
+//   a -> enumerate -> map { p -> ... }        index-element pairs
 //   a[i] -> println, "text" -> print, () -> time, scalar arithmetic
 //   (x, y) -> helper -> z              a counted-loop helper, lifted into a
 //                                      map (and the fold helpers it calls)
@@ -837,6 +838,17 @@ struct Runner {
       r.n = v.items[0].n;
       return r;
     }
+    if (n == "enumerate") {  // zip(iota n, a): pairs (index, element)
+      if (v.ty != TY_ARR && v.ty != TY_IOTA) unsupported("line %d: enumerate of a non-array", line);
+      Value idx;
+      idx.ty = TY_IOTA;
+      idx.n = v.n;
+      Value r;
+      r.ty = TY_ZIP;
+      r.items = {idx, v};
+      r.n = v.n;
+      return r;
+    }
     if (n == "widen_f32") {
       if (v.ty == TY_I32) return num_f32((float)v.i);
       unsupported("line %d: widen_f32 of a non-i32 scalar", line);
@@ -892,8 +904,21 @@ struct Runner {
                   b->kids[1]->k == Expr::NAME &&
                   ((b->kids[0]->s == L.params[0] && b->kids[1]->s == L.params[1]) ||
                    (b->kids[0]->s == L.params[1] && b->kids[1]->s == L.params[0]));
+    if (is_sum && xs.ty == TY_ARR && xs.elem == TY_I32 && seed.ty == TY_I32) {
+      // wrapping i32 addition is associative: the parallel fold is exact
+      say("fold_sum_i32 n=" + std::to_string(xs.n));
+      if (plan) return num_i32(0);
+      int32_t* out = nullptr;
+      if (cudaMalloc(&out, 4) != cudaSuccess) infra("cudaMalloc");
+      check(mapal_gpu_fold_sum_i32(ctx, seed.i, (const int32_t*)xs.ptr(), xs.n, out), "fold_sum_i32");
+      sync_point();
+      int32_t r = 0;
+      if (cudaMemcpy(&r, out, 4, cudaMemcpyDeviceToHost) != cudaSuccess) infra("cudaMemcpy");
+      cudaFree(out);
+      return num_i32(r);
+    }
     if (!is_sum || xs.ty != TY_ARR || xs.elem != TY_F32 || seed.ty != TY_F32)
-      unsupported("line %d: only the f32 sum fold runs at top level", line);
+      unsupported("line %d: only the f32 and i32 sum folds run at top level", line);
     say(std::string(fast_fold ? "fold_sum_f32" : "fold_sum_f32_strict") + " n=" + std::to_string(xs.n));
     if (plan) return num_f32(0);
     float* out = nullptr;

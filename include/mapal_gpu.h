@@ -320,6 +320,13 @@ int mapal_gpu_gather(MapalGpuCtx* ctx, const float* x, uint64_t n_x, const int32
  * within 1e-6 * sum|x| of the exact sum. */
 int mapal_gpu_fold_sum_f32(MapalGpuCtx* ctx, float seed, const float* x, uint64_t n, float* out);
 
+/* Integer sum fold out = seed + x[0] + ... + x[n-1], wrapping i32 arithmetic
+ * (eval.rs:552-569). Wrapping addition is associative and commutative, so any
+ * order gives the interpreter's left-fold result exactly: one launch of
+ * per-thread sums, a warp and block tree, and a wrapping atomic add per block.
+ * out is a device pointer to one int32. */
+int mapal_gpu_fold_sum_i32(MapalGpuCtx* ctx, int32_t seed, const int32_t* x, uint64_t n, int32_t* out);
+
 /* The sum fold in the interpreter's order: acc = seed; acc = acc + x[i] for
  * i ascending, each add rounded to f32 (eval.rs:326-359), bit-exact with the
  * interpreter and with the reference's one-thread fold kernel

@@ -452,6 +452,10 @@ class Evaluator:
             if lens[0] != lens[1]:
                 raise Unsupported("zip of different lengths")
             return V("zip", items=v.items)
+        if name == "enumerate":
+            if v.kind not in ("arr", "iota"):
+                raise Unsupported("enumerate of a non-array")
+            return V("zip", items=[V("iota", self._len(v)), v])
         if name == "widen_f32":
             if v.kind != "i32":
                 raise Unsupported("widen_f32 of non-i32")

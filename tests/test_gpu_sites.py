@@ -244,6 +244,17 @@ def test_fold_sum_strict_bit_exact(ctx, n, offset):
     assert same_bits(host(out), np.array([o.fold_sum(0.75, x[offset:])], np.float32))
 
 
+@pytest.mark.parametrize("n", [0, 1, 1000, (1 << 20) + 3, 1 << 24])
+def test_fold_sum_i32_wrapping_exact(ctx, n):
+    rng = np.random.default_rng(n)
+    x = rng.integers(-2**31, 2**31, size=n, dtype=np.int64).astype(np.int32)
+    out = torch.empty(1, dtype=torch.int32, device="cuda")
+    ctx.fold_sum_i32(dev(x), out, seed=-123)
+    want = np.int64(-123) + x.astype(np.int64).sum()
+    want = ((int(want) + 2**31) % 2**32) - 2**31
+    assert int(host(out)[0]) == want
+
+
 def test_fold_sum_strict_specials(ctx):
     out = empty_f32(1)
     ctx.fold_sum_strict(dev(np.array([1e30, -1e30, 1.0, np.float32(2.0**-30)], np.float32)), out)

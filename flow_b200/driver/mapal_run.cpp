@@ -1,6 +1,6 @@
 // mapal_run.cpp — run a Mapal program's `main` with every bulk site on the GPU.
 //
-//   mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] [--tf32x3] program.mapal
+//   mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] [--tf32x3] [--no-fuse] program.mapal
 //
 // The reference compiles a program to CUDA C++ (`emit`, crates/backends/cuda/
 // src/lib.rs:72-111) and the emitted `main` launches one generated kernel per
@@ -33,6 +33,10 @@
 // every other site runs on the first device. --tf32x3 runs matmul-shaped
 // sites on the tensor cores (3xTF32, within its stated tolerance) for programs
 // whose precision contract allows it; the default stays strict.
+// A general map body that cannot trap is deferred (elem_plan's `Apply`,
+// crates/mapal-ir/src/algo.rs:451-475): a consumer map recomputes it in its own
+// program, and its array is written only when something else reads it or a
+// clock read comes while it is live. --no-fuse writes every map site's array.
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <unistd.h>
@@ -583,6 +587,8 @@ struct DevBuf {
   }
 };
 
+struct Lazy;
+
 struct Value {
   Ty ty = TY_UNIT;
   int32_t i = 0;
@@ -594,7 +600,24 @@ struct Value {
   uint64_t n = 0;               // array / iota length
   uint64_t id = 0;              // array identity (also in plan mode)
   std::shared_ptr<DevBuf> buf;  // array storage (absent in plan mode)
-  void* ptr() const { return buf ? buf->p : nullptr; }
+  std::shared_ptr<Lazy> lazy;   // a deferred map: materialised on first ptr()
+  void* ptr() const;
+};
+
+// A map site whose body is trap-free and effect-free, held as its element law
+// instead of launched (elem_plan's `Apply`, crates/mapal-ir/src/algo.rs:
+// 451-475 and the gate `body_is_classifiable`, :1531-1545). A consumer map
+// splices `ops` into its own program and recomputes the element; the array is
+// written only if something else reads it (a site that needs the pointer, an
+// element read) or a clock read comes while it is still live.
+struct Lazy {
+  std::vector<MapalExprOp> ops;  // the body, without its store
+  std::vector<Value> arrays;     // the body's slot table
+  Ty out = TY_F32;
+  uint64_t n = 0;
+  bool consumed = false;  // spliced into a consumer at least once
+  bool done = false;      // materialised into `mat`
+  Value mat;
 };
 
 // ---- the runner ---------------------------------------------------------------------------
@@ -765,6 +788,7 @@ struct Runner {
     }
     if (a.ty != TY_ARR) unsupported("line %d: indexing a non-array", line);
     if (j < 0 || (uint64_t)j >= a.n) mapal_trap(1);
+    if (a.lazy) a.ptr();  // a deferred map is written before its element is read
     if (plan) {
       say("read element " + std::to_string(j));
       return a.elem == TY_I32 ? num_i32(0) : num_f32(0);
@@ -805,6 +829,59 @@ struct Runner {
   }
 
   // -- statements --
+
+  // Every name a statement mentions (its expressions, stage names and lambda
+  // bodies): a superset of the bindings it reads.
+  static void names_in(const EP& e, std::set<std::string>& out) {
+    if (!e) return;
+    if (e->k == Expr::NAME) out.insert(e->s);
+    for (auto& k : e->kids) names_in(k, out);
+  }
+  static void names_in(const Chain& c, std::set<std::string>& out) {
+    names_in(c.head, out);
+    for (auto& s : c.stages) {
+      if (s.k == Stage::NAMED) out.insert(s.name);
+      if (s.lam)
+        for (auto& st : s.lam->stmts) names_in(st, out);
+    }
+  }
+
+  // A site about to read an array: a deferred map is written first.
+  void need(const Value& v) {
+    if (v.lazy && !v.lazy->done) materialise(*v.lazy);
+    for (auto& it : v.items) need(it);
+  }
+
+  void keep_bufs(const Value& v) {
+    if (v.buf) kept.push_back(v.buf);
+    if (v.lazy && v.lazy->mat.buf) kept.push_back(v.lazy->mat.buf);
+    for (auto& it : v.items) keep_bufs(it);
+  }
+
+  // main's statements in order. After each one, the bindings no later
+  // statement mentions are released (their device memory is kept until exit),
+  // so a deferred map whose only reader recomputed it is never written.
+  void run_main(const std::vector<Chain>& body) {
+    std::map<std::string, size_t> last;
+    for (size_t j = 0; j < body.size(); ++j) {
+      std::set<std::string> ns;
+      names_in(body[j], ns);
+      for (auto& n : ns) last[n] = j;
+    }
+    for (size_t j = 0; j < body.size(); ++j) {
+      run_chain(body[j]);
+      for (auto it = env.begin(); it != env.end();) {
+        auto l = last.find(it->first);
+        if (l != last.end() && l->second > j) {
+          ++it;
+          continue;
+        }
+        keep_bufs(it->second);
+        it = env.erase(it);
+      }
+      settle(false);
+    }
+  }
 
   void run(const std::vector<Chain>& body) {
     for (auto& c : body) run_chain(c);
@@ -865,6 +942,7 @@ struct Runner {
     if (n == "time") {
       // the clock reads after the device drains: the elapsed time between two
       // reads covers the sites launched between them
+      settle(true);
       sync_point();
       return num_f64(mapal_time_ms());
     }
@@ -906,6 +984,7 @@ struct Runner {
                    (b->kids[0]->s == L.params[1] && b->kids[1]->s == L.params[0]));
     if (is_sum && xs.ty == TY_ARR && xs.elem == TY_I32 && seed.ty == TY_I32) {
       // wrapping i32 addition is associative: the parallel fold is exact
+      need(xs);
       say("fold_sum_i32 n=" + std::to_string(xs.n));
       if (plan) return num_i32(0);
       int32_t* out = nullptr;
@@ -919,6 +998,7 @@ struct Runner {
     }
     if (!is_sum || xs.ty != TY_ARR || xs.elem != TY_F32 || seed.ty != TY_F32)
       unsupported("line %d: only the f32 and i32 sum folds run at top level", line);
+    need(xs);
     say(std::string(fast_fold ? "fold_sum_f32" : "fold_sum_f32_strict") + " n=" + std::to_string(xs.n));
     if (plan) return num_f32(0);
     float* out = nullptr;
@@ -969,7 +1049,11 @@ struct Runner {
       if (s.k == Stage::NAMED && s.name == "widen_f32" && !widen) widen = true;
       else unsupported("line %d: map body stage", line);
     }
-    if (!widen) {
+    // a deferred producer is recomputed inside the general map body rather than
+    // written for a specialised kernel to read
+    bool deferred_input = dom.lazy && !dom.lazy->done;
+    for (auto& it : dom.items) deferred_input |= it.lazy && !it.lazy->done;
+    if (!widen && !(fuse_maps && deferred_input)) {
       if (Value r; try_gather(L.params[0], body, dom, r, line)) return r;
       if (Value r; try_move(L.params[0], body, dom, r, line)) return r;
       if (Value r; try_saxpy(L.params[0], body, dom, r, line)) return r;
@@ -1018,6 +1102,7 @@ struct Runner {
     if (b->kids[0]->k != Expr::NAME || b->kids[1]->k != Expr::NAME || b->kids[1]->s != prm) return false;
     Value x = eval(b->kids[0], line);
     if (x.ty != TY_ARR || x.elem != TY_F32) return false;
+    need(x);
     say("gather n=" + std::to_string(dom.n) + " n_x=" + std::to_string(x.n));
     out = make_array(TY_F32, dom.n);
     if (!plan) check(mapal_gpu_gather(ctx, (const float*)x.ptr(), x.n, (const int32_t*)dom.ptr(), (float*)out.ptr(), dom.n), "gather");
@@ -1166,6 +1251,8 @@ struct Runner {
     };
     fill(fa, s.a, A.n);
     fill(fbb, s.b, B.n);
+    need(A);
+    need(B);
     say(describe(s));
     if (nt_shaped(s)) return matmul_nt(s, A, B, line);
     return run_tile(s, A, B);
@@ -1316,6 +1403,7 @@ struct Runner {
     }
     if (!W || cq < 0 || cr < 0 || dom.n % (uint64_t)W) return false;
     MapalMoveSite s{(uint64_t)W, dom.n / W, (uint64_t)cq, (uint64_t)cr, a.n};
+    need(a);
     say("move_site width=" + std::to_string(W) + " rows=" + std::to_string(s.rows) + " cq=" + std::to_string(cq) +
         " cr=" + std::to_string(cr));
     out = make_array(TY_F32, dom.n);
@@ -1511,19 +1599,41 @@ struct Runner {
     std::string prm;
     const Value& dom;
     int line;
+    bool fuse = false;  // splice deferred producers instead of reading their arrays
     std::vector<MapalExprOp> ops;
     std::vector<Value> arrays;  // slot table
+    std::vector<std::shared_ptr<Lazy>> spliced;
+    bool overflow = false;  // a fused program outgrew the op or slot table
 
     int slot_of(const Value& a) {
       for (size_t s = 0; s < arrays.size(); ++s)
         if (arrays[s].id == a.id) return (int)s;
-      if (arrays.size() >= MAPAL_X_MAX_ARRAYS) unsupported("line %d: more than 8 arrays in one map body", line);
+      if (arrays.size() >= MAPAL_X_MAX_ARRAYS) {
+        if (!fuse) unsupported("line %d: more than 8 arrays in one map body", line);
+        overflow = true;
+        return 0;
+      }
       arrays.push_back(a);
       return (int)arrays.size() - 1;
     }
     void emit(uint16_t code, uint16_t slot = 0, int32_t i = 0, float f = 0) {
-      if (ops.size() >= MAPAL_X_MAX_OPS - 1) unsupported("line %d: map body too long", line);
+      if (ops.size() >= MAPAL_X_MAX_OPS - 1) {
+        if (!fuse) unsupported("line %d: map body too long", line);
+        overflow = true;
+        return;
+      }
       ops.push_back(MapalExprOp{code, slot, i, f});
+    }
+    // the producer's element law in place of a load of its element
+    Ty splice(const std::shared_ptr<Lazy>& z) {
+      for (MapalExprOp op : z->ops) {
+        const bool slotted = op.code == MAPAL_X_IN_I32 || op.code == MAPAL_X_IN_F32 ||
+                             op.code == MAPAL_X_LOAD_I32 || op.code == MAPAL_X_LOAD_F32;
+        if (slotted) op.slot = (uint16_t)slot_of(z->arrays[op.slot]);
+        emit(op.code, op.slot, op.i, op.f);
+      }
+      spliced.push_back(z);
+      return z->out;
     }
     // the element (or zip projection) pushes
     Ty push_elem(int which) {
@@ -1544,6 +1654,7 @@ struct Runner {
         emit(MAPAL_X_T_I32);
         return TY_I32;
       }
+      if (fuse && src->lazy && !src->lazy->done) return splice(src->lazy);
       int s = slot_of(*src);
       emit(src->elem == TY_F32 ? MAPAL_X_IN_F32 : MAPAL_X_IN_I32, (uint16_t)s);
       return src->elem;
@@ -1616,50 +1727,170 @@ struct Runner {
     }
   };
 
-  Value general_map(const std::string& prm, const EP& body, bool widen, const Value& dom, int line) {
-    Compiler C{*this, prm, dom, line, {}, {}};
-    Ty t = C.gen(body, TY_F32);
-    if (widen) {
-      if (t != TY_I32) unsupported("line %d: widen_f32 of a non-i32 body", line);
-      C.emit(MAPAL_X_WIDEN_I32_F32);
-      t = TY_F32;
+  // Deepest stack a program reaches (the map_expr kernel holds 16 values).
+  static int stack_depth(const std::vector<MapalExprOp>& ops) {
+    int sp = 0, top = 0;
+    for (const MapalExprOp& op : ops) {
+      switch (op.code) {
+        case MAPAL_X_T_I32: case MAPAL_X_CONST_I32: case MAPAL_X_CONST_F32:
+        case MAPAL_X_IN_I32: case MAPAL_X_IN_F32:
+          ++sp;
+          break;
+        case MAPAL_X_LOAD_I32: case MAPAL_X_LOAD_F32: case MAPAL_X_NEG_I32: case MAPAL_X_NEG_F32:
+        case MAPAL_X_WIDEN_I32_F32:
+          break;
+        default:  // the binary ops and the store pop one
+          --sp;
+      }
+      if (sp > top) top = sp;
     }
-    if (t != TY_I32 && t != TY_F32) unsupported("line %d: map body result type", line);
-    C.ops.push_back(MapalExprOp{(uint16_t)(t == TY_F32 ? MAPAL_X_STORE_F32 : MAPAL_X_STORE_I32), 0, 0, 0});
-    say("map_expr n=" + std::to_string(dom.n) + " ops=" + std::to_string(C.ops.size()) +
-        " arrays=" + std::to_string(C.arrays.size()));
-    Value out = make_array(t, dom.n);
+    return top;
+  }
+
+  // Whether consumers may recompute a body in place of loading its result: no
+  // Index read (it could trap index_oob) and no i32 division or remainder by
+  // anything but a nonzero literal (div_zero). Float arithmetic never traps,
+  // and a body holds no print, clock or loop, so it is also effect-free.
+  static bool trap_free(const std::vector<MapalExprOp>& ops) {
+    for (size_t k = 0; k < ops.size(); ++k) {
+      const uint16_t c = ops[k].code;
+      if (c == MAPAL_X_LOAD_I32 || c == MAPAL_X_LOAD_F32) return false;
+      if ((c == MAPAL_X_DIV_I32 || c == MAPAL_X_REM_I32) &&
+          !(k > 0 && ops[k - 1].code == MAPAL_X_CONST_I32 && ops[k - 1].i != 0))
+        return false;
+    }
+    return true;
+  }
+
+  static constexpr int kMapStack = 16;
+  bool fuse_maps = true;                        // --no-fuse: every map site writes its array
+  std::vector<std::shared_ptr<Lazy>> pending;  // deferred maps not yet written
+  std::vector<std::shared_ptr<DevBuf>> kept;   // dead arrays, freed at exit (cudaFree waits for the device)
+
+  // Launch a deferred map: its body plus the store, into a new array.
+  void materialise(Lazy& z) {
+    if (z.done) return;
+    z.done = true;
+    for (auto& a : z.arrays) need(a);
+    std::vector<MapalExprOp> prog = z.ops;
+    prog.push_back(MapalExprOp{(uint16_t)(z.out == TY_F32 ? MAPAL_X_STORE_F32 : MAPAL_X_STORE_I32), 0, 0, 0});
+    say("map_expr n=" + std::to_string(z.n) + " ops=" + std::to_string(prog.size()) +
+        " arrays=" + std::to_string(z.arrays.size()));
+    Value out = make_array(z.out, z.n);
     if (!plan) {
       std::vector<const void*> ptrs;
       std::vector<uint64_t> lens;
-      for (auto& a : C.arrays) {
+      for (auto& a : z.arrays) {
         ptrs.push_back(a.ptr());
         lens.push_back(a.n);
       }
-      check(mapal_gpu_map_expr(ctx, C.ops.data(), (uint32_t)C.ops.size(), ptrs.data(), lens.data(),
-                               (uint32_t)C.arrays.size(), out.ptr(), dom.n),
+      check(mapal_gpu_map_expr(ctx, prog.data(), (uint32_t)prog.size(), ptrs.data(), lens.data(),
+                               (uint32_t)z.arrays.size(), out.ptr(), z.n),
             "map_expr");
     }
-    return out;
+    z.mat = out;
+  }
+
+  // After a statement (clock = false) or before a clock read (clock = true).
+  // A deferred map that nothing holds any more is dropped when a consumer
+  // recomputed it and written otherwise, so its work still runs where the
+  // program put it; before a clock read every live one is written, so the
+  // time between two reads covers the sites issued between them.
+  void settle(bool clock) {
+    std::vector<std::shared_ptr<Lazy>> keep;
+    for (auto& z : pending) {
+      const bool dead = z.use_count() == 1;
+      if (!z->done && !(dead && z->consumed) && (dead || clock)) materialise(*z);
+      if (z->done) {
+        if (z->mat.buf) kept.push_back(z->mat.buf);
+      } else if (!dead) {
+        keep.push_back(z);
+      }
+    }
+    pending.swap(keep);
+  }
+
+  Value general_map(const std::string& prm, const EP& body, bool widen, const Value& dom, int line) {
+    for (int pass = 0;; ++pass) {
+      // pass 0 splices deferred producers; pass 1 (if the fused program is too
+      // long, too deep or has too many arrays) reads their arrays instead
+      Compiler C{*this, prm, dom, line};
+      C.fuse = fuse_maps && pass == 0;
+      Ty t = C.gen(body, TY_F32);
+      if (widen) {
+        if (t != TY_I32) unsupported("line %d: widen_f32 of a non-i32 body", line);
+        C.emit(MAPAL_X_WIDEN_I32_F32);
+        t = TY_F32;
+      }
+      if (t != TY_I32 && t != TY_F32) unsupported("line %d: map body result type", line);
+      if (C.fuse && (C.overflow || stack_depth(C.ops) > kMapStack)) continue;
+      for (auto& z : C.spliced) z->consumed = true;
+      const std::string fused = C.spliced.empty() ? "" : " fused=" + std::to_string(C.spliced.size());
+      if (fuse_maps && dom.n > 0 && dom.n <= (1ull << 31) && trap_free(C.ops)) {
+        auto z = std::make_shared<Lazy>();
+        z->ops = C.ops;
+        z->arrays = C.arrays;
+        z->out = t;
+        z->n = dom.n;
+        say("map_expr n=" + std::to_string(dom.n) + " ops=" + std::to_string(C.ops.size() + 1) +
+            " arrays=" + std::to_string(C.arrays.size()) + fused + " deferred");
+        pending.push_back(z);
+        Value v;
+        v.ty = TY_ARR;
+        v.elem = t;
+        v.n = dom.n;
+        v.id = next_id++;
+        v.lazy = z;
+        return v;
+      }
+      for (auto& a : C.arrays) need(a);
+      C.ops.push_back(MapalExprOp{(uint16_t)(t == TY_F32 ? MAPAL_X_STORE_F32 : MAPAL_X_STORE_I32), 0, 0, 0});
+      say("map_expr n=" + std::to_string(dom.n) + " ops=" + std::to_string(C.ops.size()) +
+          " arrays=" + std::to_string(C.arrays.size()) + fused);
+      Value out = make_array(t, dom.n);
+      if (!plan) {
+        std::vector<const void*> ptrs;
+        std::vector<uint64_t> lens;
+        for (auto& a : C.arrays) {
+          ptrs.push_back(a.ptr());
+          lens.push_back(a.n);
+        }
+        check(mapal_gpu_map_expr(ctx, C.ops.data(), (uint32_t)C.ops.size(), ptrs.data(), lens.data(),
+                                 (uint32_t)C.arrays.size(), out.ptr(), dom.n),
+              "map_expr");
+      }
+      return out;
+    }
   }
 };
+
+Runner* g_runner = nullptr;
+
+void* Value::ptr() const {
+  if (lazy) {
+    if (!lazy->done) g_runner->materialise(*lazy);
+    return lazy->mat.buf ? lazy->mat.buf->p : nullptr;
+  }
+  return buf ? buf->p : nullptr;
+}
 
 }  // namespace
 
 int main(int argc, char** argv) {
-  bool plan = false, fast_fold = false, tf32x3 = false;
+  bool plan = false, fast_fold = false, tf32x3 = false, no_fuse = false;
   int device = 0, gpus = 1;
   const char* path = nullptr;
   for (int a = 1; a < argc; ++a) {
     if (!strcmp(argv[a], "--plan")) plan = true;
     else if (!strcmp(argv[a], "--fast-fold")) fast_fold = true;
     else if (!strcmp(argv[a], "--tf32x3")) tf32x3 = true;
+    else if (!strcmp(argv[a], "--no-fuse")) no_fuse = true;
     else if (!strcmp(argv[a], "--device") && a + 1 < argc) device = atoi(argv[++a]);
     else if (!strcmp(argv[a], "--gpus") && a + 1 < argc) gpus = atoi(argv[++a]);
     else path = argv[a];
   }
   if (!path) {
-    fprintf(stderr, "usage: mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] [--tf32x3] program.mapal\n");
+    fprintf(stderr, "usage: mapal-run [--device D] [--gpus N] [--plan] [--fast-fold] [--tf32x3] [--no-fuse] program.mapal\n");
     return 2;
   }
   if (gpus < 1 || device < 0 || device + gpus > 32) {
@@ -1686,6 +1917,8 @@ int main(int argc, char** argv) {
   R.dev0 = device;
   R.plan = plan;
   R.fast_fold = fast_fold;
+  R.fuse_maps = !no_fuse;
+  g_runner = &R;
   mapal_time_ms();  // start the process clock, as the reference's runtime does on first use
   if (!plan) {
     int have = 0;
@@ -1700,10 +1933,12 @@ int main(int argc, char** argv) {
     check(mapal_gpu_set_stream(R.ctx, 0, nullptr), "set_stream");
     check(mapal_gpu_set_sync(R.ctx, 0), "set_sync");
   }
-  R.run(body);
+  R.run_main(body);
   if (R.ctx) {
     check(mapal_gpu_synchronize(R.ctx), "synchronize");
     R.env.clear();
+    R.pending.clear();
+    R.kept.clear();
     mapal_gpu_ctx_destroy(R.ctx);
   }
   fflush(stdout);

@@ -76,10 +76,10 @@ def test_time_mark_matching():
 
 # ---- the driver's site plan ---------------------------------------------------------
 
-def _plan(src: str, tmp_path) -> subprocess.CompletedProcess:
+def _plan(src: str, tmp_path, *flags: str) -> subprocess.CompletedProcess:
     f = tmp_path / "p.mapal"
     f.write_text(src)
-    return subprocess.run([DRIVER, "--plan", str(f)], capture_output=True, text=True, timeout=60)
+    return subprocess.run([DRIVER, "--plan", *flags, str(f)], capture_output=True, text=True, timeout=60)
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -101,9 +101,16 @@ def _driver_built():
     (P.gather(1000), "gather n=1000 n_x=1000"),
 ])
 def test_plan_recognises_sites(prog, site, tmp_path):
-    r = _plan(prog, tmp_path)
+    # the recogniser alone: with fusion on, a site whose input is a deferred
+    # map becomes one general map body that recomputes the input instead
+    r = _plan(prog, tmp_path, "--no-fuse")
     assert r.returncode == 0, r.stderr
     assert site in r.stdout.split("\n")
+
+
+def test_plan_gather_recomputes_its_index_array(tmp_path):
+    lines = _plan(P.gather(1000), tmp_path).stdout.split("\n")
+    assert lines[1:3] == ["map_expr n=1000 ops=8 arrays=0 deferred", "map_expr n=1000 ops=9 arrays=1 fused=1"]
 
 
 @pytest.mark.parametrize("path", PROGRAMS, ids=os.path.basename)
@@ -115,12 +122,47 @@ def test_plan_every_program(path):
     assert bool(calls) == ("-> map" in open(path).read())
 
 
+FUSE_SRC = ("fn main() {\n 100 -> iota -> d;\n d -> map { i -> i * i % 7 -> widen_f32 } -> f;\n"
+            " f -> map { x -> x / 3.0 - x % 2.0 } -> g;\n g[5] -> println;\n}\n")
+
+
 def test_plan_general_body_uses_map_expr(tmp_path):
-    r = _plan("fn main() {\n 100 -> iota -> d;\n d -> map { i -> i * i % 7 -> widen_f32 } -> f;\n"
-              " f -> map { x -> x / 3.0 - x % 2.0 } -> g;\n g[5] -> println;\n}\n", tmp_path)
+    r = _plan(FUSE_SRC, tmp_path, "--no-fuse")
     assert r.returncode == 0, r.stderr
-    assert "map_expr n=100 ops=7 arrays=0" in r.stdout  # i, i, *, 7, %, widen, store
-    assert "map_expr n=100 ops=8 arrays=1" in r.stdout
+    assert r.stdout.split("\n")[:2] == ["map_expr n=100 ops=7 arrays=0",  # i, i, *, 7, %, widen, store
+                                        "map_expr n=100 ops=8 arrays=1"]
+
+
+def test_plan_fuses_producer_into_consumer(tmp_path):
+    # f's body (trap-free: % by a nonzero literal) is recomputed at both of g's
+    # uses of x; f is never written, g is written when its element is read
+    r = _plan(FUSE_SRC, tmp_path)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.split("\n")[:4] == ["map_expr n=100 ops=7 arrays=0 deferred",
+                                        "map_expr n=100 ops=18 arrays=0 fused=2 deferred",
+                                        "map_expr n=100 ops=18 arrays=0", "read element 5"]
+
+
+def test_plan_fusion_gates(tmp_path):
+    lines = _plan(open(os.path.join(HERE, "programs", "fused_chain.mapal")).read(), tmp_path).stdout.split("\n")
+    # a three-stage chain becomes one program
+    assert "map_expr n=70001 ops=43 arrays=0 fused=3 deferred" in lines
+    # a clock read writes the live deferred map first
+    assert lines.index("map_expr n=70001 ops=6 arrays=0") < lines.index("map_expr n=70001 ops=4 arrays=1 deferred")
+    # too deep / too long once fused: the consumer reads the producer's array
+    assert "map_expr n=70001 ops=18 arrays=1 deferred" in lines
+    assert "map_expr n=70001 ops=16 arrays=1 deferred" in lines
+    # bodies that can trap are launched where they stand, never deferred
+    trap = _plan("fn main() {\n 10 -> iota -> d;\n d -> map { i -> 100 / (i - 3) } -> q;\n"
+                 " d -> map { i -> q[9 - i] } -> r;\n}\n", tmp_path).stdout.split("\n")
+    assert trap[:2] == ["map_expr n=10 ops=6 arrays=0", "map_expr n=10 ops=5 arrays=1"]
+
+
+def test_plan_dead_unconsumed_map_still_runs(tmp_path):
+    r = _plan("fn main() {\n 64 -> iota -> d;\n d -> map { i -> i + 1 } -> unused;\n \"x\" -> println;\n}\n",
+              tmp_path)
+    assert r.stdout.split("\n")[:3] == ["map_expr n=64 ops=4 arrays=0 deferred", "map_expr n=64 ops=4 arrays=0",
+                                        "println"]
 
 
 def test_plan_lifts_counted_loops(tmp_path):

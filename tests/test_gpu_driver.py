@@ -18,13 +18,13 @@ DRIVER = os.path.join(os.path.dirname(HERE), "flow_b200", "mapal-run")
 PROGRAMS = sorted(glob.glob(os.path.join(HERE, "programs", "*.mapal")))
 
 
-def _run(path: str) -> subprocess.CompletedProcess:
-    return subprocess.run([DRIVER, path], capture_output=True, text=True, timeout=300)
+def _run(path: str, *flags: str) -> subprocess.CompletedProcess:
+    return subprocess.run([DRIVER, *flags, path], capture_output=True, text=True, timeout=300)
 
 
-def _check(path: str, src: str):
+def _check(path: str, src: str, *flags: str):
     want, want_rc = expected(src)
-    r = _run(path)
+    r = _run(path, *flags)
     assert r.returncode == want_rc, (r.returncode, r.stdout, r.stderr)
     assert matches(r.stdout, want), (r.stdout, want)
     if want_rc == 101:
@@ -34,6 +34,12 @@ def _check(path: str, src: str):
 @pytest.mark.parametrize("path", PROGRAMS, ids=os.path.basename)
 def test_program(path):
     _check(path, open(path).read())
+
+
+@pytest.mark.parametrize("path", PROGRAMS, ids=os.path.basename)
+def test_program_unfused(path):
+    # every map site writes its array: the same stdout as the fused run
+    _check(path, open(path).read(), "--no-fuse")
 
 
 @pytest.mark.parametrize("name,src", [

@@ -598,7 +598,11 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
     s = torch.empty(1, dtype=torch.float32, device="cuda")
     ctx.gen(x, 3, lo, fb.U01)
     ms = d.max(time_launches(torch, stream, lambda: ctx.fold_sum_sharded([x], [s]), lambda: None, 3))
-    big["sum_2^30"] = {"ms": ms, "gbs": 4 * n / (ms * 1e-3) / 1e9, "collective": "NCCL all-reduce f64"}
+    comb = ctx.sum_combine()
+    big["sum_2^30"] = {"ms": ms, "gbs": 4 * n / (ms * 1e-3) / 1e9,
+                       "collective": ("none (one rank)" if d.world == 1 else
+                                      "f64 partials exchanged over peer memory inside the fold kernel"
+                                      if comb == 1 else "NCCL all-reduce f64")}
     del x
     ng = 1 << 28
     lo, hi = fb.shard_range(ng, d.world, d.rank)

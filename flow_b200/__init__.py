@@ -199,6 +199,12 @@ class Context:
         _check(lib().mapal_gpu_ctx_world(self._h, ctypes.byref(n), ctypes.byref(r)))
         return n.value, r.value
 
+    def sum_combine(self) -> int:
+        """1: sharded sums combine over peer memory; -1: NCCL all-reduce; 0: not yet decided."""
+        m = ctypes.c_int()
+        _check(lib().mapal_gpu_ctx_sum_combine(self._h, ctypes.byref(m)))
+        return m.value
+
     def stream(self, local: int = 0) -> int:
         s = ctypes.c_void_p()
         _check(lib().mapal_gpu_get_stream(self._h, local, ctypes.byref(s)))

@@ -34,6 +34,7 @@ SIGNATURES: dict[str, tuple] = {
     "mapal_gpu_ctx_destroy": (_int, [_vp]),
     "mapal_gpu_ctx_local_devices": (_int, [_vp, _c.POINTER(_int)]),
     "mapal_gpu_ctx_world": (_int, [_vp, _c.POINTER(_int), _c.POINTER(_int)]),
+    "mapal_gpu_ctx_sum_combine": (_int, [_vp, _c.POINTER(_int)]),
     "mapal_gpu_profile": (_int, [_vp, _int, _c.POINTER(GpuProfile)]),
     "mapal_gpu_get_stream": (_int, [_vp, _int, _pp]),
     "mapal_gpu_set_stream": (_int, [_vp, _int, _vp]),

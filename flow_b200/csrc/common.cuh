@@ -17,7 +17,7 @@ typedef struct ncclComm* ncclComm_t;
 struct NcclId {
   char internal[128];
 };
-enum NcclDtype { kNcclFloat32 = 7, kNcclFloat64 = 8 };
+enum NcclDtype { kNcclUint8 = 1, kNcclFloat32 = 7, kNcclFloat64 = 8 };
 enum NcclOp { kNcclSum = 0 };
 
 struct NcclApi {
@@ -32,8 +32,36 @@ struct NcclApi {
   int (*GroupStart)() = nullptr;
   int (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(int) = nullptr;
+  int (*AllGather)(const void*, void*, size_t, int, ncclComm_t, cudaStream_t) = nullptr;
 };
 NcclApi* nccl_api();  // loads on first use; check ->loaded
+
+// ---- peer exchange --------------------------------------------------------------
+// The sharded sum combines its per-rank partials over peer memory inside the
+// fold kernel: every rank stores its partial into every rank's block and
+// raises its flag there, then waits for every rank's flag in its own block and
+// adds the partials in rank order. Values are double-buffered by the parity of
+// a per-call epoch, so a rank one call ahead never overwrites a value that a
+// slower rank has yet to read.
+constexpr int kMaxPeers = 8;  // one NVSwitch node
+struct PeerSlot {
+  double v;
+  unsigned long long epoch;  // the call that wrote v
+};
+struct PeerBlock {
+  PeerSlot val[2][kMaxPeers];          // [epoch parity][source rank]
+  unsigned long long flag[kMaxPeers];  // last epoch each source rank published
+};
+struct PeerArgs {
+  PeerBlock* blk[kMaxPeers];  // every rank's block as this device addresses it
+  PeerBlock* own;             // this device's block
+  int nranks;
+  int rank;
+  unsigned long long epoch;
+  unsigned* trap;  // 0x100: a wait gave up; 0x200: ranks out of step
+};
+constexpr unsigned kPeerTimeout = 0x100u;
+constexpr unsigned kPeerOutOfStep = 0x200u;
 
 // ---- context ------------------------------------------------------------------
 
@@ -63,6 +91,11 @@ struct DeviceSlot {
   std::vector<cudaEvent_t> host_events;
   void* stage = nullptr;
   size_t stage_bytes = 0;
+  // Peer exchange (set up by the first sharded sum): this device's block and
+  // every rank's block as mapped here (peer access or an IPC mapping).
+  PeerBlock* xblk = nullptr;
+  PeerBlock* peer_blk[kMaxPeers] = {};
+  bool peer_ipc[kMaxPeers] = {};  // opened with cudaIpcOpenMemHandle
   MapalGpuProfile prof{};
 };
 
@@ -71,6 +104,8 @@ struct MapalGpuCtx {
   int nranks = 1;  // ranks of the communicator
   int rank0 = 0;   // global rank of local device 0
   bool sync = true;
+  int peer_state = 0;              // 0 not tried, 1 peer combine ready, -1 NCCL only
+  unsigned long long xepoch = 0;   // sharded-sum calls made through the peer combine
 };
 
 // Blocks per fold launch is fixed per n (deterministic); this bounds it.
@@ -127,6 +162,13 @@ int launch_gather(cudaStream_t s, int sms, const float* x, uint64_t n_x, const i
 int launch_fold_sum(cudaStream_t s, int sms, const float* x, uint64_t n, float seed, double* partials,
                     unsigned* counter, float* out_f32, double* out_f64);
 int launch_finalize_sum(cudaStream_t s, const double* total, float seed, float* out);
+// The fold with the cross-rank combine in its last block (out = seed + the
+// rank-ordered sum of every rank's partial).
+int launch_fold_sum_peer(cudaStream_t s, int sms, const float* x, uint64_t n, float seed, double* partials,
+                         unsigned* counter, float* out, const PeerArgs& P);
+// Map every rank's exchange block (collective on the first call; sets
+// ctx->peer_state, -1 when any rank cannot map its peers).
+int peer_setup(MapalGpuCtx* ctx);
 int launch_matmul_strict(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
                          uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed);
 int launch_matmul_strict_ex(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,

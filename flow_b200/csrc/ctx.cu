@@ -7,6 +7,7 @@
 // library returns the status to its caller, which owns the process.
 #include <dlfcn.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <atomic>
@@ -69,6 +70,7 @@ NcclApi* nccl_api() {
     g_nccl.GroupStart = (int (*)())sym("ncclGroupStart");
     g_nccl.GroupEnd = (int (*)())sym("ncclGroupEnd");
     g_nccl.GetErrorString = (const char* (*)(int))sym("ncclGetErrorString");
+    g_nccl.AllGather = (int (*)(const void*, void*, size_t, int, ncclComm_t, cudaStream_t))sym("ncclAllGather");
     if (!ok) {
       g_nccl.error = "libnccl.so.2 lacks a required symbol";
       return;
@@ -178,6 +180,9 @@ static void free_slot(DeviceSlot& d) {
   }
   for (cudaEvent_t e : d.host_events) cudaEventDestroy(e);
   cudaFree(d.stage);
+  for (int q = 0; q < kMaxPeers; ++q)
+    if (d.peer_ipc[q]) cudaIpcCloseMemHandle(d.peer_blk[q]);
+  cudaFree(d.xblk);
   if (d.own_stream) cudaStreamDestroy(d.own_stream);
   d = DeviceSlot{};
 }
@@ -298,6 +303,12 @@ extern "C" int mapal_gpu_ctx_world(MapalGpuCtx* ctx, int* nranks, int* rank) {
   return 0;
 }
 
+extern "C" int mapal_gpu_ctx_sum_combine(MapalGpuCtx* ctx, int* mode) {
+  if (!ctx || !mode) return set_error(MAPAL_ERR_INVALID, "null argument");
+  *mode = ctx->peer_state;
+  return 0;
+}
+
 extern "C" int mapal_gpu_profile(MapalGpuCtx* ctx, int local, MapalGpuProfile* out) {
   if (!out) return set_error(MAPAL_ERR_INVALID, "out is null");
   MAPAL_TRY(enter(ctx, local));
@@ -349,7 +360,9 @@ int drain(DeviceSlot& d) {
     MAPAL_CUDA(cudaStreamSynchronize(d.stream));
     if (kind == 1) return set_error(MAPAL_TRAP_DIV_ZERO, "mapal trap: div_zero");
     if (kind == 2) return set_error(MAPAL_TRAP_INDEX_OOB, "mapal trap: index_oob");
-    if (kind & 0x100u) return set_error(MAPAL_ERR_TIMEOUT, "a bounded device wait gave up (tensor-core pipeline)");
+    if (kind & kPeerOutOfStep)
+      return set_error(MAPAL_ERR_NCCL, "ranks out of step in the sharded-sum exchange (a rank skipped a call)");
+    if (kind & 0x100u) return set_error(MAPAL_ERR_TIMEOUT, "a bounded device wait gave up");
     return set_error(MAPAL_ERR_CUDA, "trap flag holds an unknown kind");
   }
   return 0;
@@ -446,5 +459,105 @@ int nccl_broadcast_f32_on(MapalGpuCtx* ctx, float* const* buf, size_t offset, si
   }
   rc = n->GroupEnd();
   if (rc) return nccl_fail(rc, "ncclGroupEnd");
+  return 0;
+}
+
+// ---- peer exchange setup ---------------------------------------------------------------
+//
+// One process over several devices: peer access between every pair, and the
+// blocks are plain device pointers. One process per device: each rank exports
+// its block as an IPC handle, the handles are all-gathered over NCCL and
+// opened. Every rank then agrees (an NCCL sum of the ranks that succeeded), so
+// either all ranks combine over peer memory or all use ncclAllReduce.
+// MAPAL_GPU_PEER_COMBINE=0 in any rank's environment selects ncclAllReduce.
+int peer_setup(MapalGpuCtx* ctx) {
+  if (ctx->peer_state) return 0;
+  const int R = ctx->nranks, L = (int)ctx->dev.size();
+  if (R < 2) {
+    ctx->peer_state = -1;
+    return 0;
+  }
+  NcclApi* n = nccl_api();
+  if (!n->loaded) return set_error(MAPAL_ERR_NCCL, n->error);
+  const char* env = getenv("MAPAL_GPU_PEER_COMBINE");
+  if (L != R && L != 1) {  // not a layout the context constructors make
+    ctx->peer_state = -1;
+    return 0;
+  }
+  bool ok = R <= kMaxPeers && !(env && env[0] == '0');
+  constexpr size_t kBlockBytes = 64 << 10;
+  static_assert(sizeof(PeerBlock) <= kBlockBytes, "peer block");
+  for (auto& d : ctx->dev) {
+    MAPAL_CUDA(cudaSetDevice(d.device));
+    if (!d.xblk) {
+      MAPAL_CUDA(cudaMalloc(&d.xblk, kBlockBytes));
+      MAPAL_CUDA(cudaMemset(d.xblk, 0, kBlockBytes));
+      MAPAL_CUDA(cudaDeviceSynchronize());
+    }
+  }
+  if (L == R) {
+    // every rank is a local device of this process
+    for (int i = 0; i < L && ok; ++i) {
+      MAPAL_CUDA(cudaSetDevice(ctx->dev[i].device));
+      for (int j = 0; j < L && ok; ++j) {
+        ctx->dev[i].peer_blk[j] = ctx->dev[j].xblk;
+        if (i == j) continue;
+        int can = 0;
+        cudaDeviceCanAccessPeer(&can, ctx->dev[i].device, ctx->dev[j].device);
+        cudaError_t e = can ? cudaDeviceEnablePeerAccess(ctx->dev[j].device, 0) : cudaErrorPeerAccessUnsupported;
+        if (e == cudaErrorPeerAccessAlreadyEnabled) e = cudaSuccess;
+        if (e != cudaSuccess) ok = false;
+        cudaGetLastError();
+      }
+    }
+    ctx->peer_state = ok ? 1 : -1;
+    return 0;
+  }
+  // one device per process: exchange IPC handles
+  DeviceSlot& d = ctx->dev[0];
+  const int me = ctx->rank0;
+  cudaIpcMemHandle_t mine{};
+  if (ok && cudaIpcGetMemHandle(&mine, d.xblk) != cudaSuccess) {
+    ok = false;
+    cudaGetLastError();
+  }
+  if (n->AllGather == nullptr) return set_error(MAPAL_ERR_NCCL, "libnccl lacks ncclAllGather");
+  const size_t hb = sizeof(cudaIpcMemHandle_t);
+  std::vector<uint8_t> all(hb * R);
+  uint8_t* dbuf = nullptr;
+  MAPAL_CUDA(cudaMalloc(&dbuf, hb * R));
+  MAPAL_CUDA(cudaMemcpy(dbuf + hb * me, &mine, hb, cudaMemcpyHostToDevice));
+  int rc = n->AllGather(dbuf + hb * me, dbuf, hb, kNcclUint8, d.comm, d.stream);
+  if (rc) {
+    cudaFree(dbuf);
+    return nccl_fail(rc, "ncclAllGather");
+  }
+  MAPAL_CUDA(cudaStreamSynchronize(d.stream));
+  MAPAL_CUDA(cudaMemcpy(all.data(), dbuf, hb * R, cudaMemcpyDeviceToHost));
+  MAPAL_CUDA(cudaFree(dbuf));
+  for (int q = 0; q < R && ok; ++q) {
+    if (q == me) {
+      d.peer_blk[q] = d.xblk;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, all.data() + hb * q, hb);
+    void* p = nullptr;
+    if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      ok = false;
+      cudaGetLastError();
+      break;
+    }
+    d.peer_blk[q] = (PeerBlock*)p;
+    d.peer_ipc[q] = true;
+  }
+  // agreement: the number of ranks that mapped every peer
+  double flag = ok ? 1.0 : 0.0;
+  MAPAL_CUDA(cudaMemcpy(d.fold_total, &flag, sizeof flag, cudaMemcpyHostToDevice));
+  double* tot[1] = {d.fold_total};
+  MAPAL_TRY(nccl_allreduce_f64(ctx, tot, 1));
+  MAPAL_CUDA(cudaStreamSynchronize(d.stream));
+  MAPAL_CUDA(cudaMemcpy(&flag, d.fold_total, sizeof flag, cudaMemcpyDeviceToHost));
+  ctx->peer_state = flag == (double)R ? 1 : -1;
   return 0;
 }

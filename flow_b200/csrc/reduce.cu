@@ -32,11 +32,68 @@ __device__ __forceinline__ double block_sum(double v, double* smem) {
   return t;  // valid in thread 0
 }
 
-template <bool kVec>
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// A rank that has not published after this long is reported, not waited for.
+constexpr uint64_t kPeerWaitNs = 10ull * 1000 * 1000 * 1000;
+
+// Warp 0 of the last block: lane q stores this rank's partial into rank q's
+// block and raises its flag there, then waits (bounded) for rank q's flag in
+// this device's block. Lane 0 adds the partials in rank order, so every rank
+// writes the same value.
+__device__ void peer_combine(double mine, float seed, float* out, const PeerArgs& P) {
+  const int q = threadIdx.x;
+  const int par = (int)(P.epoch & 1);
+  unsigned err = 0;
+  double v = 0.0;
+  if (q < P.nranks) {
+    PeerBlock* dst = P.blk[q];
+    volatile PeerSlot* slot = &dst->val[par][P.rank];
+    slot->v = mine;
+    slot->epoch = P.epoch;
+    st_release_sys(&dst->flag[P.rank], P.epoch);
+    const uint64_t t0 = global_ns();
+    while (ld_acquire_sys(&P.own->flag[q]) < P.epoch) {
+      if (global_ns() - t0 > kPeerWaitNs) {
+        err = kPeerTimeout;
+        break;
+      }
+      __nanosleep(32);
+    }
+    if (!err) {
+      volatile const PeerSlot* src = &P.own->val[par][q];
+      if (src->epoch != P.epoch) err = kPeerOutOfStep;
+      v = src->v;
+    }
+  }
+  err = __reduce_or_sync(0xffffffffu, err);
+  double total = 0.0;
+  for (int r = 0; r < P.nranks; ++r) total += __shfl_sync(0xffffffffu, v, r);
+  if (q == 0) {
+    if (err)
+      atomicOr(P.trap, err);
+    else
+      *out = (float)((double)seed + total);
+  }
+}
+
+template <bool kVec, bool kPeer>
 __global__ void __launch_bounds__(kThreads) fold_sum_kernel(const float* __restrict__ x, uint64_t n,
                                                             float seed, double* partials,
                                                             unsigned* counter, float* out_f32,
-                                                            double* out_f64) {
+                                                            double* out_f64, const __grid_constant__ PeerArgs P) {
   __shared__ double smem[kWarps];
   __shared__ bool last;
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -85,6 +142,16 @@ __global__ void __launch_bounds__(kThreads) fold_sum_kernel(const float* __restr
   double t = 0.0;
   for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) t += __ldcg(partials + b);
   double total = block_sum(t, smem);
+  if (kPeer) {
+    __shared__ double rank_total;
+    if (threadIdx.x == 0) {
+      rank_total = total;
+      *counter = 0u;
+    }
+    __syncthreads();
+    if (threadIdx.x < 32) peer_combine(rank_total, seed, out_f32, P);
+    return;
+  }
   if (threadIdx.x == 0) {
     if (out_f64) *out_f64 = total;
     if (out_f32) *out_f32 = (float)((double)seed + total);
@@ -107,9 +174,26 @@ int launch_fold_sum(cudaStream_t s, int sms, const float* x, uint64_t n, float s
   if (cap > (uint64_t)kFoldMaxBlocks) cap = kFoldMaxBlocks;
   unsigned grid = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
   if (n >= 4 && aligned16(x))
-    fold_sum_kernel<true><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64);
+    fold_sum_kernel<true, false><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64,
+                                                           PeerArgs{});
   else
-    fold_sum_kernel<false><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64);
+    fold_sum_kernel<false, false><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out_f32, out_f64,
+                                                            PeerArgs{});
+  count_launch();
+  return 0;
+}
+
+int launch_fold_sum_peer(cudaStream_t s, int sms, const float* x, uint64_t n, float seed, double* partials,
+                         unsigned* counter, float* out, const PeerArgs& P) {
+  // the same grid rule as launch_fold_sum: the rank's partial is the same tree
+  uint64_t want = (n + (uint64_t)kThreads * 16 - 1) / ((uint64_t)kThreads * 16);
+  uint64_t cap = (uint64_t)sms * 4;
+  if (cap > (uint64_t)kFoldMaxBlocks) cap = kFoldMaxBlocks;
+  unsigned grid = (unsigned)(want < 1 ? 1 : (want > cap ? cap : want));
+  if (n >= 4 && aligned16(x))
+    fold_sum_kernel<true, true><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out, nullptr, P);
+  else
+    fold_sum_kernel<false, true><<<grid, kThreads, 0, s>>>(x, n, seed, partials, counter, out, nullptr, P);
   count_launch();
   return 0;
 }

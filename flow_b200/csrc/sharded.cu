@@ -123,6 +123,28 @@ extern "C" int mapal_gpu_saxpy_sharded(MapalGpuCtx* ctx, float a, const float* c
 extern "C" int mapal_gpu_fold_sum_f32_sharded(MapalGpuCtx* ctx, float seed, const float* const* x,
                                               const uint64_t* n, float* const* out) {
   MAPAL_TRY(check_arrays(ctx, x, n, out));
+  for (int i = 0; i < (int)ctx->dev.size(); ++i)
+    if ((n[i] && !x[i]) || !out[i]) return set_error(MAPAL_ERR_INVALID, "null shard");
+  MAPAL_TRY(peer_setup(ctx));
+  if (ctx->peer_state == 1) {
+    // one kernel per rank: the fold, then the partials exchanged over peer
+    // memory and added in rank order by the fold's last block
+    const unsigned long long epoch = ++ctx->xepoch;
+    for (int i = 0; i < (int)ctx->dev.size(); ++i) {
+      MAPAL_TRY(enter(ctx, i));
+      DeviceSlot& d = ctx->dev[i];
+      PeerArgs P{};
+      for (int q = 0; q < ctx->nranks; ++q) P.blk[q] = d.peer_blk[q];
+      P.own = d.xblk;
+      P.nranks = ctx->nranks;
+      P.rank = ctx->rank0 + i;
+      P.epoch = epoch;
+      P.trap = d.trap;
+      MAPAL_TRY(launch_fold_sum_peer(d.stream, d.prof.sm_count, x[i], n[i], seed, d.fold_partials,
+                                     d.fold_counter, out[i], P));
+    }
+    return finish_all(ctx, true);
+  }
   std::vector<double*> totals(ctx->dev.size());
   for (int i = 0; i < (int)ctx->dev.size(); ++i) {
     MAPAL_TRY(enter(ctx, i));

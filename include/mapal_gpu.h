@@ -403,10 +403,23 @@ int mapal_gpu_shard_range(uint64_t n, int nranks, int r, uint64_t* lo, uint64_t*
 int mapal_gpu_saxpy_sharded(MapalGpuCtx* ctx, float a, const float* const* x,
                             const float* const* y0, float* const* y, const uint64_t* n);
 
-/* Sum over contiguous shards: one f64 partial per rank, combined by an NCCL
- * all-reduce; every local device receives the f32 result in out[d]. */
+/* Sum over contiguous shards: one f64 partial per rank; every local device
+ * receives the f32 result seed + (sum of the partials) in out[d]. The
+ * partials are combined inside the fold kernel over peer memory (each rank
+ * stores its partial into every rank's exchange block; the sum is taken in
+ * rank order, so every rank holds the same value); when some rank cannot map
+ * its peers (or MAPAL_GPU_PEER_COMBINE=0), by an NCCL all-reduce instead. The
+ * first call on a multi-rank context is collective setup (IPC handles
+ * all-gathered over NCCL). A rank whose peers do not publish within 10 s
+ * returns MAPAL_ERR_TIMEOUT. Replaces the CUDA backend's one-thread fold
+ * (crates/backends/cuda/src/kernel.rs:1484-1642) for a sharded array. */
 int mapal_gpu_fold_sum_f32_sharded(MapalGpuCtx* ctx, float seed, const float* const* x,
                                    const uint64_t* n, float* const* out);
+
+/* How the context's sharded sum combines partials: 0 = not decided yet (no
+ * sharded sum called), 1 = over peer memory in the fold kernel, -1 = NCCL
+ * all-reduce (one rank, or peers not mappable). */
+int mapal_gpu_ctx_sum_combine(MapalGpuCtx* ctx, int* mode);
 
 /* Broadcast n floats from global rank `root` into buf[d] on every device. */
 int mapal_gpu_broadcast_f32(MapalGpuCtx* ctx, float* const* buf, uint64_t n, int root);

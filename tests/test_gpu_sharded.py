@@ -63,6 +63,35 @@ def test_fold_sum_sharded(ctx):
     assert abs(got - o.sum_f64(0.25, x)) <= 1e-6 * (o.sum_abs_f64(x) + 0.25)
 
 
+@pytest.mark.skipif(NDEV < 2, reason="needs two GPUs")
+def test_fold_sum_sharded_peer_combine_repeated(ctx, monkeypatch):
+    # Back-to-back calls reuse the exchange slots by epoch parity: every call's
+    # result is the same on every device and matches the ncclAllReduce path
+    # within the reordering tolerance.
+    D = devs()
+    n = (1 << 20) + 333
+    warm = [torch.ones(8, device=f"cuda:{d}") for d in D]
+    ctx.fold_sum_sharded(warm, [torch.empty(1, device=f"cuda:{d}") for d in D])  # maps the peers
+    monkeypatch.setenv("MAPAL_GPU_PEER_COMBINE", "0")  # the reference context takes ncclAllReduce
+    ref_ctx = fb.Context(D)
+    try:
+        for call in range(12):
+            x = o.gen(n, 40 + call, 0, o.U01 if call % 2 else o.U11)
+            spans = [fb.shard_range(n, len(D), i) for i in range(len(D))]
+            xs = [on(d, x[lo:hi]) for d, (lo, hi) in zip(D, spans)]
+            outs = [torch.empty(1, dtype=torch.float32, device=f"cuda:{d}") for d in D]
+            ctx.fold_sum_sharded(xs, outs, seed=0.5 * call)
+            vals = {float(t.cpu().item()) for t in outs}
+            assert len(vals) == 1, (call, vals)
+            got = vals.pop()
+            assert abs(got - o.sum_f64(0.5 * call, x)) <= 1e-6 * (o.sum_abs_f64(x) + 0.5 * call)
+            ref = [torch.empty(1, dtype=torch.float32, device=f"cuda:{d}") for d in D]
+            ref_ctx.fold_sum_sharded(xs, ref, seed=0.5 * call)
+            assert abs(got - float(ref[0].cpu().item())) <= 1e-6 * (o.sum_abs_f64(x) + 0.5 * call)
+    finally:
+        ref_ctx.close()
+
+
 def test_broadcast_then_gather_sharded(ctx):
     nx, n = 1 << 20, (1 << 20) + 3
     x = o.gen(nx, 3, 0)
@@ -119,6 +148,13 @@ def _rank_worker(rank, world, port, q):
         out = torch.empty(1, dtype=torch.float32, device=f"cuda:{rank}")
         ctx.fold_sum_sharded([on(rank, x[lo:hi])], [out], seed=0.0)
         s = float(out.cpu().item())
+        # repeated calls through the peer exchange: the same value every time
+        xr = on(rank, x[lo:hi])
+        again = set()
+        for _ in range(9):
+            ctx.fold_sum_sharded([xr], [out], seed=0.0)
+            again.add(float(out.cpu().item()))
+        ok_repeat = again == {s}
         M, N, K = 300, 200, 150
         A, B = o.gen(M * K, 7, 0), o.gen(K * N, 7, M * K)
         mlo, mhi = fb.shard_range(M, world, rank)
@@ -129,7 +165,7 @@ def _rank_worker(rank, world, port, q):
         ok_mm = np.array_equal(C.cpu().numpy().view(np.uint32), want.view(np.uint32))
         ok_sum = abs(s - o.sum_f64(0.0, x)) <= 1e-6 * o.sum_abs_f64(x)
         ctx.close()
-        q.put((rank, s, ok_sum, ok_mm))
+        q.put((rank, s, ok_sum and ok_repeat, ok_mm))
     finally:
         dist.destroy_process_group()
 

@@ -369,10 +369,12 @@ def run_ours(args) -> int:
         got = C[:n].cpu().numpy()
         check = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
 
-    # e2e through the public API with host buffers: every rank calls the
-    # host-array entry on its row block with its own pinned copy of B, so the
-    # uploads (A block and B), the multiply and the download of its C block
-    # overlap in k-range phases on each GPU; the device result is the check.
+    # e2e through the public API with host buffers: the host-array entry on
+    # this rank's row block, its pinned copy of B beside it. The uploads, the
+    # multiply and the download of the C block overlap in k-range phases; over
+    # several ranks each rank uploads only its slice of every phase's B rows
+    # and the slices cross NVLink (mapal_gpu_matmul_f32_host_sharded). The
+    # device result is the check.
     e2e = None
     if not args.no_e2e:
         A_h = torch.empty(m * n, dtype=torch.float32, pin_memory=True)
@@ -386,8 +388,12 @@ def run_ours(args) -> int:
         del b_full
         e_steps = max(2, min(args.steps, 5))
 
-        def e2e_step():
-            ctx.matmul_host(local_site, A_h, B_h, C_h, mode)
+        if d.world > 1:
+            def e2e_step():
+                ctx.matmul_host_sharded(local_site, [A_h], [B_h], [C_h], [m], mode)
+        else:
+            def e2e_step():
+                ctx.matmul_host(local_site, A_h, B_h, C_h, mode)
 
         e2e_step()
         ctx.synchronize()
@@ -402,12 +408,16 @@ def run_ours(args) -> int:
         torch.cuda.synchronize()
         e_ms = d.max(ev[0].elapsed_time(ev[1]) / e_steps)
         same = d.sum(0.0 if torch.equal(C_h[:m * n], C[:m * n].cpu()) else 1.0) == 0.0
-        h2d = d.sum(float(m * n * 4 + n * n * 4))
+        shared_b = d.world > 1 and mode == fb.STRICT and n >= 512
+        b_up = n * n * 4 // d.world if shared_b else n * n * 4  # this rank's share of B (about 1/R)
+        h2d = d.sum(float(m * n * 4 + b_up))
         d2h = d.sum(float(m * n * 4))
         e2e = {"value": flops / (e_ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": e_ms,
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": e_steps,
                "matches_device_result": bool(same),
-               "path": "pinned host A block, B -> mapal_gpu_matmul_f32_host on every rank -> pinned host C block"}
+               "path": ("pinned host A block + 1/R of B per rank -> mapal_gpu_matmul_f32_host_sharded "
+                        "(B slices gathered over NVLink) -> pinned host C block" if shared_b else
+                        "pinned host A, B -> mapal_gpu_matmul_f32_host -> pinned host C")}
 
     pk = peaks()
     sm_mhz = clk["sm_mhz"] if clk else pk["sm_max_mhz"]

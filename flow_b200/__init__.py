@@ -284,6 +284,12 @@ class Context:
         numpy arrays): copies in, multiply and copy out overlap in row blocks."""
         _check(lib().mapal_gpu_matmul_f32_host(self._h, ctypes.byref(site), _ptr(A), _ptr(B), _ptr(C), mode))
 
+    def matmul_host_sharded(self, site: TileSite, As, Bs, Cs, rows: Sequence[int], mode: int = STRICT) -> None:
+        """The host-array matmul over the context's ranks: As[d] / Cs[d] are the local
+        device's row blocks in host memory, Bs[d] a host copy of the whole B."""
+        _check(lib().mapal_gpu_matmul_f32_host_sharded(self._h, ctypes.byref(site), _arr(As), _arr(Bs), _arr(Cs),
+                                                       _u64s(rows), mode))
+
     def tile_site(self, site: TileSite, a, b, out, mode: int = STRICT) -> None:
         _check(lib().mapal_gpu_tile_site_f32(self._h, ctypes.byref(site), _ptr(a), _ptr(b), _ptr(out), mode))
 

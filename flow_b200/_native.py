@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "mapal_gpu_conv2d_3x3_f32": (_int, [_vp, _c.POINTER(TileSite), _vp, _vp, _vp]),
     "mapal_gpu_matmul_f32": (_int, [_vp, _c.POINTER(TileSite), _vp, _vp, _vp, _int]),
     "mapal_gpu_matmul_f32_host": (_int, [_vp, _c.POINTER(TileSite), _vp, _vp, _vp, _int]),
+    "mapal_gpu_matmul_f32_host_sharded": (_int, [_vp, _c.POINTER(TileSite), _vp, _vp, _vp, _vp, _int]),
     "mapal_gpu_tile_site_f32": (_int, [_vp, _c.POINTER(TileSite), _vp, _vp, _vp, _int]),
     "mapal_gpu_shard_range": (_int, [_u64, _int, _int, _pu64, _pu64]),
     "mapal_gpu_saxpy_sharded": (_int, [_vp, _f32, _pp, _pp, _pp, _pu64]),

@@ -88,6 +88,7 @@ struct DeviceSlot {
   // events and a growable device staging buffer, all created on first use.
   cudaStream_t h2d_stream = nullptr;
   cudaStream_t d2h_stream = nullptr;
+  cudaStream_t aux_stream = nullptr;  // a second compute stream: row blocks alternate with `stream`
   std::vector<cudaEvent_t> host_events;
   void* stage = nullptr;
   size_t stage_bytes = 0;

@@ -172,7 +172,7 @@ static void free_slot(DeviceSlot& d) {
     cudaStreamDestroy(d.comm_stream);
   }
   for (cudaEvent_t e : d.events) cudaEventDestroy(e);
-  for (cudaStream_t s : {d.h2d_stream, d.d2h_stream}) {
+  for (cudaStream_t s : {d.h2d_stream, d.d2h_stream, d.aux_stream}) {
     if (s) {
       cudaStreamSynchronize(s);
       cudaStreamDestroy(s);

@@ -3,7 +3,8 @@
 // The reference is one process with no multi-GPU path. Its bulk sites split
 // naturally, and only where they do does this library shard them:
 //  * saxpy: contiguous equal shards, no exchange;
-//  * sum:   contiguous shards, one f64 partial per rank, one NCCL all-reduce;
+//  * sum:   contiguous shards, one f64 partial per rank, combined over peer
+//           memory in the fold kernel (or one NCCL all-reduce);
 //  * gather: idx sharded, x replicated (NCCL broadcast, done once by the caller);
 //  * matmul: A row blocks, B replicated by NCCL broadcast, C row blocks stay put.
 // A context spans either several devices of one process (arrays hold one
@@ -16,8 +17,6 @@ int nccl_broadcast_f32(MapalGpuCtx* ctx, float* const* buf, size_t count, int ro
 int tile_site_on(MapalGpuCtx* ctx, int local, const MapalTileSite* site, const float* a, const float* b,
                  float* out, int mode);
 
-namespace {
-
 // Finish a multi-device call: launch errors, then (sync mode) every device's
 // completion and trap flag. The first nonzero status wins.
 int finish_all(MapalGpuCtx* ctx, bool trap_capable) {
@@ -29,6 +28,8 @@ int finish_all(MapalGpuCtx* ctx, bool trap_capable) {
   }
   return first;
 }
+
+namespace {
 
 int check_arrays(MapalGpuCtx* ctx, const void* a, const void* b, const void* c) {
   if (!ctx) return set_error(MAPAL_ERR_INVALID, "ctx is null");

@@ -386,6 +386,19 @@ int mapal_gpu_matmul_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const floa
 int mapal_gpu_matmul_f32_host(MapalGpuCtx* ctx, const MapalTileSite* site, const float* A,
                               const float* B, float* C, int mode);
 
+/* The host-array matmul site over the context's ranks: local device d owns
+ * m[d] rows of A and C (A[d], C[d] point at the block's first row, in host
+ * memory) and B[d] is a host copy of the whole B (the same pointer may serve
+ * several local devices). In strict mode with K >= 512 each rank uploads only
+ * its 1/nranks of every k-phase's B rows, and the ranks broadcast their slices
+ * to one another over NVLink on a comm stream while the previous phase
+ * multiplies; otherwise every rank runs mapal_gpu_matmul_f32_host on its block.
+ * Collective: every rank calls it with the same site. Results equal the
+ * one-device call's rows. */
+int mapal_gpu_matmul_f32_host_sharded(MapalGpuCtx* ctx, const MapalTileSite* site,
+                                      const float* const* A, const float* const* B, float* const* C,
+                                      const uint64_t* m, int mode);
+
 /* Any TileSite: dispatches to the matmul, FIR or conv2d kernel when the record
  * has that shape, else runs the generic one-thread-per-cell site kernel
  * (bit-exact, the rung-0 shape). mode applies to matmul-shaped sites. */

@@ -113,3 +113,31 @@ def test_host_rejects_bad_records(ctx):
     with pytest.raises(fb.Unsupported):
         ctx.matmul_host(fb.fir_site(10, 3), np.zeros(3, np.float32), np.zeros(12, np.float32),
                         np.zeros(10, np.float32))
+
+
+NDEV = torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+@pytest.mark.skipif(NDEV < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("M,N,K,ldb,bbase", [(1000, 300, 1000, None, 0),    # B slices gathered over NVLink
+                                             (700, 257, 777, 263, 5),       # padded, offset B; ragged slices
+                                             (3, 129, 640, None, 0),        # ranks with no rows still serve B
+                                             (500, 200, 100, None, 0)])     # shallow K: per-rank full upload
+def test_strict_host_sharded_bit_exact(M, N, K, ldb, bbase):
+    D = list(range(min(NDEV, 8)))
+    ctx = fb.Context(D)
+    try:
+        s = _site(M, N, K, ldb=ldb, bbase=bbase, seed=0.25)
+        A, B = _inputs(s, seed=21)
+        rc, want = o.tile_site(o.TileSite.from_buffer_copy(bytes(s)), A, B)
+        assert rc == 0
+        spans = [fb.shard_range(M, len(D), i) for i in range(len(D))]
+        Bh = torch.from_numpy(B).pin_memory()
+        As = [torch.from_numpy(A[lo * K:hi * K].copy()).pin_memory() for lo, hi in spans]
+        Cs = [torch.full(((hi - lo) * N,), float("nan"), dtype=torch.float32).pin_memory() for lo, hi in spans]
+        for _ in range(2):  # the second call reuses the staging and the comm stream
+            ctx.matmul_host_sharded(s, As, [Bh] * len(D), Cs, [hi - lo for lo, hi in spans])
+            got = np.concatenate([c.numpy() for c in Cs])
+            assert same_bits(got, want), first_diff(got, want)
+    finally:
+        ctx.close()

@@ -163,6 +163,14 @@ def _rank_worker(rank, world, port, q):
         ctx.matmul_sharded(fb.matmul_site(M, N, K), [on(rank, A[mlo * K:mhi * K])], [Bd], [C], [mhi - mlo])
         want = o.matmul(A, B, M, N, K, row0=mlo, row1=mhi).reshape(M, N)[mlo:mhi].ravel()
         ok_mm = np.array_equal(C.cpu().numpy().view(np.uint32), want.view(np.uint32))
+        # the host-array entry: this rank's A and C blocks, B's slices gathered over NVLink
+        K2 = 640
+        A2, B2 = o.gen(M * K2, 8, 0), o.gen(K2 * N, 8, M * K2)
+        Ch = np.full((mhi - mlo) * N, np.nan, np.float32)
+        ctx.matmul_host_sharded(fb.matmul_site(M, N, K2), [A2[mlo * K2:mhi * K2].copy()], [B2], [Ch], [mhi - mlo])
+        ctx.synchronize()
+        want2 = o.matmul(A2, B2, M, N, K2, row0=mlo, row1=mhi).reshape(M, N)[mlo:mhi].ravel()
+        ok_mm = ok_mm and np.array_equal(Ch.view(np.uint32), want2.view(np.uint32))
         ok_sum = abs(s - o.sum_f64(0.0, x)) <= 1e-6 * o.sum_abs_f64(x)
         ctx.close()
         q.put((rank, s, ok_sum and ok_repeat, ok_mm))

@@ -58,7 +58,8 @@ struct PeerArgs {
   int nranks;
   int rank;
   unsigned long long epoch;
-  unsigned* trap;  // 0x100: a wait gave up; 0x200: ranks out of step
+  unsigned long long wait_ns;  // how long to wait for a rank that has not published
+  unsigned* trap;              // 0x100: a wait gave up; 0x200: ranks out of step
 };
 constexpr unsigned kPeerTimeout = 0x100u;
 constexpr unsigned kPeerOutOfStep = 0x200u;
@@ -107,6 +108,7 @@ struct MapalGpuCtx {
   bool sync = true;
   int peer_state = 0;              // 0 not tried, 1 peer combine ready, -1 NCCL only
   unsigned long long xepoch = 0;   // sharded-sum calls made through the peer combine
+  unsigned long long peer_wait_ns = 10ull * 1000 * 1000 * 1000;  // MAPAL_GPU_PEER_WAIT_MS
 };
 
 // Blocks per fold launch is fixed per n (deterministic); this bounds it.

@@ -469,7 +469,8 @@ int nccl_broadcast_f32_on(MapalGpuCtx* ctx, float* const* buf, size_t offset, si
 // its block as an IPC handle, the handles are all-gathered over NCCL and
 // opened. Every rank then agrees (an NCCL sum of the ranks that succeeded), so
 // either all ranks combine over peer memory or all use ncclAllReduce.
-// MAPAL_GPU_PEER_COMBINE=0 in any rank's environment selects ncclAllReduce.
+// MAPAL_GPU_PEER_COMBINE=0 in any rank's environment selects ncclAllReduce;
+// MAPAL_GPU_PEER_WAIT_MS bounds the wait for the other ranks (default 10 s).
 int peer_setup(MapalGpuCtx* ctx) {
   if (ctx->peer_state) return 0;
   const int R = ctx->nranks, L = (int)ctx->dev.size();
@@ -480,6 +481,10 @@ int peer_setup(MapalGpuCtx* ctx) {
   NcclApi* n = nccl_api();
   if (!n->loaded) return set_error(MAPAL_ERR_NCCL, n->error);
   const char* env = getenv("MAPAL_GPU_PEER_COMBINE");
+  if (const char* w = getenv("MAPAL_GPU_PEER_WAIT_MS")) {
+    const long long ms = atoll(w);
+    if (ms > 0 && ms <= 600000) ctx->peer_wait_ns = (unsigned long long)ms * 1000000ull;
+  }
   if (L != R && L != 1) {  // not a layout the context constructors make
     ctx->peer_state = -1;
     return 0;

@@ -46,9 +46,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
   return v;
 }
 
-// A rank that has not published after this long is reported, not waited for.
-constexpr uint64_t kPeerWaitNs = 10ull * 1000 * 1000 * 1000;
-
 // Warp 0 of the last block: lane q stores this rank's partial into rank q's
 // block and raises its flag there, then waits (bounded) for rank q's flag in
 // this device's block. Lane 0 adds the partials in rank order, so every rank
@@ -66,7 +63,7 @@ __device__ void peer_combine(double mine, float seed, float* out, const PeerArgs
     st_release_sys(&dst->flag[P.rank], P.epoch);
     const uint64_t t0 = global_ns();
     while (ld_acquire_sys(&P.own->flag[q]) < P.epoch) {
-      if (global_ns() - t0 > kPeerWaitNs) {
+      if (global_ns() - t0 > P.wait_ns) {  // a rank that has not published is reported, not waited for
         err = kPeerTimeout;
         break;
       }

@@ -140,6 +140,7 @@ extern "C" int mapal_gpu_fold_sum_f32_sharded(MapalGpuCtx* ctx, float seed, cons
       P.nranks = ctx->nranks;
       P.rank = ctx->rank0 + i;
       P.epoch = epoch;
+      P.wait_ns = ctx->peer_wait_ns;
       P.trap = d.trap;
       MAPAL_TRY(launch_fold_sum_peer(d.stream, d.prof.sm_count, x[i], n[i], seed, d.fold_partials,
                                      d.fold_counter, out[i], P));

@@ -424,7 +424,7 @@ int mapal_gpu_saxpy_sharded(MapalGpuCtx* ctx, float a, const float* const* x,
  * its peers (or MAPAL_GPU_PEER_COMBINE=0), by an NCCL all-reduce instead. The
  * first call on a multi-rank context is collective setup (IPC handles
  * all-gathered over NCCL). A rank whose peers do not publish within 10 s
- * returns MAPAL_ERR_TIMEOUT. Replaces the CUDA backend's one-thread fold
+ * (MAPAL_GPU_PEER_WAIT_MS, read at that setup) returns MAPAL_ERR_TIMEOUT. Replaces the CUDA backend's one-thread fold
  * (crates/backends/cuda/src/kernel.rs:1484-1642) for a sharded array. */
 int mapal_gpu_fold_sum_f32_sharded(MapalGpuCtx* ctx, float seed, const float* const* x,
                                    const uint64_t* n, float* const* out);

@@ -197,3 +197,53 @@ def test_one_process_per_gpu():
         assert p.exitcode == 0
     assert len({r[1] for r in res}) == 1
     assert all(r[2] and r[3] for r in res), res
+
+
+def _skip_worker(rank, world, port, q):
+    # the exchange's wait is bounded: a rank that never makes the call leaves
+    # the other rank with MAPAL_ERR_TIMEOUT after MAPAL_GPU_PEER_WAIT_MS, not a hang
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), MAPAL_GPU_PEER_WAIT_MS="1000",
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        obj = [fb.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        ctx = fb.Context((rank,), rank=rank, nranks=world, nccl_id=obj[0])
+        x = torch.ones(1000, device=f"cuda:{rank}")
+        out = torch.empty(1, device=f"cuda:{rank}")
+        ctx.fold_sum_sharded([x], [out])  # both ranks: setup and one exchange
+        first = float(out.cpu().item())
+        status = None
+        if rank == 0:  # rank 1 skips the second call
+            try:
+                ctx.fold_sum_sharded([x], [out])
+            except fb.MapalInfraError as e:
+                status = e.status
+        dist.barrier()
+        q.put((rank, first, ctx.sum_combine(), status))
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(NDEV < 2, reason="needs two GPUs")
+def test_peer_exchange_wait_is_bounded():
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctxm = mp.get_context("spawn")
+    q = ctxm.Queue()
+    procs = [ctxm.Process(target=_skip_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert [r[1] for r in res] == [2000.0, 2000.0]
+    assert [r[2] for r in res] == [1, 1]  # the peer combine was in use
+    assert res[0][3] == fb.ERR_TIMEOUT and res[1][3] is None

@@ -18,8 +18,9 @@
 // block of A and C, and B is needed whole by every rank: instead of every rank
 // pushing all of B across its own PCIe link, each rank uploads 1/R of every
 // k-phase's B rows and the ranks broadcast their slices to one another over
-// NVLink (an all-gather of unequal slices: one ncclBroadcast per owner, in one
-// group) on a comm stream, between the upload and the multiply of that phase.
+// NVLink on a comm stream, between the upload and the multiply of that phase
+// (one in-place ncclAllGather when the slices are equal whole rows of a dense
+// B, else one ncclBroadcast per owner in one group).
 #include "common.cuh"
 
 int finish_all(MapalGpuCtx* ctx, bool trap_capable);
@@ -294,11 +295,20 @@ extern "C" int mapal_gpu_matmul_f32_host_sharded(MapalGpuCtx* ctx, const MapalTi
                                      d.h2d_stream));
       MAPAL_CUDA(cudaEventRecord(ev[3 + 2 * c], d.h2d_stream));
     }
-    // the phase's B rows, gathered: every owner broadcasts its slice
+    // the phase's B rows, gathered: one in-place all-gather when every rank's
+    // slice is the same whole number of dense rows, else every owner
+    // broadcasts its slice
+    const bool equal = ldb == N && kc % (uint64_t)R == 0;
     int rc = nc->GroupStart();
     if (rc) return set_error(MAPAL_ERR_NCCL, "ncclGroupStart failed");
     for (int i = 0; i < L && !rc; ++i) {
       DeviceSlot& d = ctx->dev[i];
+      if (equal) {
+        const uint64_t per = kc / (uint64_t)R * N;
+        float* base = dB[i] + k0 * N;
+        rc = nc->AllGather(base + per * (uint64_t)(ctx->rank0 + i), base, per, kNcclFloat32, d.comm, d.comm_stream);
+        continue;
+      }
       for (int r = 0; r < R && !rc; ++r) {
         uint64_t t0, t1;
         b_slice(k0, kc, r, R, &t0, &t1);
@@ -308,7 +318,7 @@ extern "C" int mapal_gpu_matmul_f32_host_sharded(MapalGpuCtx* ctx, const MapalTi
       }
     }
     const int rc2 = nc->GroupEnd();
-    if (rc || rc2) return set_error(MAPAL_ERR_NCCL, "ncclBroadcast of a B slice failed");
+    if (rc || rc2) return set_error(MAPAL_ERR_NCCL, "gathering a phase's B slices failed");
     for (int i = 0; i < L; ++i) {
       DeviceSlot& d = ctx->dev[i];
       MAPAL_TRY(enter(ctx, i));

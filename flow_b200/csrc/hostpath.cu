@@ -3,7 +3,8 @@
 //
 // The reference's emitted program keeps arrays on the device and moves host
 // data across with one blocking cudaMemcpy per array (crates/backends/cuda/
-// src/func.rs, the H2D / D2H seams of DESIGN BC1). Here a caller holding A, B
+// src/func.rs, the H2D / D2H seams; BC1 of the reference's
+// docs/components/backend-cuda/DESIGN.md). Here a caller holding A, B
 // and C in host memory makes one call: B goes up first (every row of C needs
 // all of it), then A streams up in row blocks on a copy stream while earlier
 // blocks multiply on the context stream, and each finished block of C streams

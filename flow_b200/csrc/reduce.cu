@@ -2,7 +2,8 @@
 // (benches/shapes/reduce_1048576.mapal:10).
 //
 // The reference runs every top-level fold as one device thread
-// (<<<1,1>>>, crates/backends/cuda/src/kernel.rs:1484-1642; DESIGN BC4),
+// (<<<1,1>>>, crates/backends/cuda/src/kernel.rs:1484-1642; BC4 of the
+// reference's docs/components/backend-cuda/DESIGN.md),
 // because an f32 left fold is only bit-exact in sequence (ADR-0028 keeps f32
 // folds sequential-pinned). This site is the one place the library trades
 // bit-exactness for parallelism, under a stated tolerance: one launch, every

@@ -1,7 +1,7 @@
 """ctypes view of the CPU oracle (oracle/mapal_oracle.c).
 
-TEST INFRASTRUCTURE ONLY: the checker that tests/, the smoke check and the
-bench's CPU-baseline leg compare against. The product (flow_b200 and
+TEST INFRASTRUCTURE ONLY: the reference results that tests/, the smoke check
+and the bench's CPU-baseline leg compare against. The product (flow_b200 and
 libmapal_gpu) never imports this package.
 """
 from __future__ import annotations

@@ -1,6 +1,6 @@
 /*
  * mapal_oracle.c — CPU restatement of the Mapal interpreter for the bulk-site
- * classes (TEST INFRASTRUCTURE ONLY: the checker, never the product).
+ * classes (TEST INFRASTRUCTURE ONLY: the oracle, never the product).
  *
  * Build flags matter: -ffp-contract=off -fno-fast-math, so every float `+`
  * and `*` below is one separately rounded IEEE binary32 operation, as Rust's

@@ -2,7 +2,7 @@
  * mapal_oracle.h — CPU restatement of the Mapal interpreter's semantics for
  * the bulk-site classes that libmapal_gpu accelerates.
  *
- * TEST INFRASTRUCTURE ONLY. This is the checker: only tests/, the smoke
+ * TEST INFRASTRUCTURE ONLY. This is the oracle: only tests/, the smoke
  * check and the bench's CPU-baseline leg load it. No product code path
  * calls it, and libmapal_gpu has no CPU fallback to it.
  *

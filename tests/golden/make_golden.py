@@ -15,7 +15,7 @@ Sources, all the reference's own:
     benches/shapes/ladder2_baseline.cpp, benches/shapes/shapes_baseline.cpp),
     compiled unmodified from the reference tree into oracle/_ref/ and run
     here: their printed probe values for the shapes the GPU kernels cover.
-The fixture is committed; the GPU box never reads the reference tree.
+The fixture is committed; GPU test runs never read the reference tree.
 """
 from __future__ import annotations
 

@@ -1,7 +1,7 @@
 """Generate tests/golden/reference_outputs.json from the reference itself.
 
-Run in a container that has the reference tree (default /root/reference, or
-$MAPAL_REFERENCE) after `make -C oracle ref`:
+Run where the reference tree is at hand ($MAPAL_REFERENCE, else a checkout
+named `reference` beside this repository) after `make -C oracle ref`:
 
     python tests/golden/make_golden.py
 
@@ -28,7 +28,9 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("MAPAL_REFERENCE", "/root/reference")
+# The reference tree: $MAPAL_REFERENCE, else a checkout named `reference` beside
+# this repository.
+REF = os.environ.get("MAPAL_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 REF_BIN = os.path.join(ROOT, "oracle", "_ref")
 
 
@@ -109,6 +111,70 @@ def shapes() -> list[dict]:
     return out
 
 
+# The reference's own bench programs that the GPU driver must run unmodified:
+# every benches/shapes source, the f32 cap matmuls, the counted-loop matmuls and
+# the examples inside the bench subset. They are copied byte for byte into
+# tests/golden/mapal/<dir>/ (test inputs, never product code).
+PROGRAM_GLOBS = [("shapes", "benches/shapes", lambda f: f.endswith(".mapal")),
+                 ("matmul", "benches/matmul", lambda f: re.fullmatch(r"matmul\d+(_cap_f32)?\.mapal", f)),
+                 ("examples", "examples", lambda f: f in ("matmul4_loop.mapal", "matmul4096.mapal",
+                                                          "vector_add.mapal", "zip_demo.mapal"))]
+# Programs whose interpreter run is too long for the oracle evaluator here (or
+# that it does not parse: counted loops): their expected output is the
+# published known answer of the same product (results.csv; the loop and cap
+# forms compute every cell in the same k order).
+KNOWN_ANSWER_LEG = {"cap": "flow-cuda-cap-f32", "loop": "flow-cuda"}
+
+
+def _known_answer(leg: str, n: int) -> tuple[int, int] | None:
+    with open(os.path.join(REF, "benches/matmul/results.csv")) as f:
+        for rec in csv.reader(f):
+            if len(rec) >= 5 and rec[0] == leg and int(rec[1]) == n:
+                m = re.match(r"out=(-?\d+)/(-?\d+)", rec[4])
+                return int(m.group(1)), int(m.group(2))
+    return None
+
+
+def reference_programs() -> list[dict]:
+    sys.path.insert(0, ROOT)
+    from oracle.mapal_eval import Unsupported, expected
+
+    out_dir = os.path.join(HERE, "mapal")
+    cases = []
+    for sub, rel, keep in PROGRAM_GLOBS:
+        os.makedirs(os.path.join(out_dir, sub), exist_ok=True)
+        for name in sorted(os.listdir(os.path.join(REF, rel))):
+            if not keep(name):
+                continue
+            src = open(os.path.join(REF, rel, name), "rb").read()
+            with open(os.path.join(out_dir, sub, name), "wb") as f:
+                f.write(src)
+            text = src.decode()
+            m = re.fullmatch(r"matmul(\d+)(_cap_f32)?\.mapal", name)
+            n = int(m.group(1)) if m else None
+            case = {"file": f"{sub}/{name}", "source": f"{rel}/{name}"}
+            if m and (n >= 2048 or not m.group(2)):
+                c0_clast = _known_answer(KNOWN_ANSWER_LEG["cap"], n) or \
+                    _known_answer(KNOWN_ANSWER_LEG["loop"], n)
+                case.update({"expected": f"{c0_clast[0]}\n{c0_clast[1]}\n", "rc": 0,
+                             "expected_from": f"benches/matmul/results.csv N={n}"})
+                if "time" in text:
+                    case["expected"] += "iter ms=\x00time\x00\n"
+            else:
+                try:
+                    want, rc = expected(text)
+                    case.update({"expected": want, "rc": rc, "expected_from": "oracle evaluator"})
+                except Unsupported:
+                    km = re.search(r"matmul(\d+)", name)
+                    ka = _known_answer(KNOWN_ANSWER_LEG["loop"], int(km.group(1))) if km else None
+                    if ka is None:
+                        raise
+                    case.update({"expected": f"{ka[0]}\n{ka[1]}\n", "rc": 0,
+                                 "expected_from": f"benches/matmul/results.csv N={km.group(1)}"})
+            cases.append(case)
+    return cases
+
+
 def main() -> int:
     if not os.path.isdir(os.path.join(REF, "benches")):
         print(f"reference tree not found at {REF}", file=sys.stderr)
@@ -120,6 +186,7 @@ def main() -> int:
         "cpp_mt": cpp_mt(),
         "ladder2": ladder2(),
         "shapes": shapes(),
+        "reference_programs": reference_programs(),
     }
     path = os.path.join(HERE, "reference_outputs.json")
     with open(path, "w") as f:

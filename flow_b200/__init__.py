@@ -309,6 +309,14 @@ class Context:
         n = _u64s([o.numel() for o in outs])
         _check(lib().mapal_gpu_gather_sharded(self._h, _arr(xs), xs[0].numel(), _arr(idxs), _arr(outs), n))
 
+    def probe_mma_peak(self, kind: int = 0, iters: int = 4096) -> float:
+        """Measured tensor-pipe rate in TFLOP/s of the 3xTF32 GEMM's MMA shape
+        (kind 0: tf32; kind 1: the bf16 form of the same shape), operands
+        resident in shared memory, one CTA per SM."""
+        out = ctypes.c_double()
+        _check(lib().mapal_gpu_probe_mma_peak(self._h, kind, iters, ctypes.byref(out)))
+        return out.value
+
     def matmul_sharded(self, site: TileSite, As, Bs, Cs, rows: Sequence[int], root: int = 0,
                        mode: int = STRICT) -> None:
         _check(lib().mapal_gpu_matmul_f32_sharded(self._h, ctypes.byref(site), _arr(As), _arr(Bs),

@@ -323,6 +323,102 @@ __global__ void reduce_parts_kernel(const float* __restrict__ part, float* __res
   }
 }
 
+// ---- tensor-pipe probe ---------------------------------------------------------------------
+//
+// The roofline of the 3xTF32 GEMM is the tensor pipe's TF32 rate, which no
+// datasheet figure gives for this part at its operating clock: this kernel
+// measures it. One CTA per SM issues the GEMM's own MMA (M128 N256, operands
+// K-major with the 64-byte swizzle in shared memory, f32 accumulator in TMEM)
+// back to back with no memory traffic at all: `iters` rounds of 6 MMAs (two
+// 8-deep k-steps x three products, as one stage of the GEMM). kind 1 issues
+// the bf16 form of the same instruction shape (kind::f16, K16: the same
+// 32 bytes of each operand row per MMA), to check the method against the
+// measured cuBLAS bf16 rate.
+constexpr uint32_t kIdescBf16 = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                ((uint32_t)(BM >> 4) << 24);
+constexpr int kProbeThreads = 128;
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kIdescBf16), "r"(accumulate));
+}
+
+__global__ void __launch_bounds__(kProbeThreads, 1) probe_mma_kernel(int iters, int kind, unsigned* flag, float* sink) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  // two operand sets (hi, lo) as in one GEMM stage: A 2 x 8 KiB, B 2 x 16 KiB
+  uint32_t* words = reinterpret_cast<uint32_t*>(base);
+  __shared__ uint64_t done;
+  __shared__ uint32_t tmem_base;
+  for (int i = threadIdx.x; i < kStageBytes / 4; i += blockDim.x) {
+    // finite values of either type: a bounded hash in [-1, 1) as f32, whose
+    // 16-bit halves are ordinary bf16 values too
+    uint32_t h = (uint32_t)i * 2654435761u + 12345u;
+    h ^= h >> 13;
+    words[i] = __float_as_uint((float)(h & 0xFFFF) * (1.0f / 32768.0f) - 1.0f) & 0xFFFFE000u;
+  }
+  const int warp = threadIdx.x / 32;
+  if (threadIdx.x == 0) {
+    mbar_init(&done, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(&tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_base;
+  if (threadIdx.x == 0) {
+    const uint64_t ahi = smem_desc(base), alo = smem_desc(base + kATile);
+    const uint64_t bhi = smem_desc(base + 2 * kATile), blo = smem_desc(base + 2 * kATile + kBTile);
+    for (int it = 0; it < iters; ++it) {
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        const uint64_t adv = (uint64_t)((kk * 32) >> 4);
+        if (kind == 0) {
+          mma_tf32(tmem, ahi + adv, bhi + adv, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32(tmem, ahi + adv, blo + adv, 1u);
+          mma_tf32(tmem, alo + adv, bhi + adv, 1u);
+        } else {
+          mma_bf16(tmem, ahi + adv, bhi + adv, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16(tmem, ahi + adv, blo + adv, 1u);
+          mma_bf16(tmem, alo + adv, bhi + adv, 1u);
+        }
+      }
+    }
+    mma_commit(&done);
+    // bounded: a wait that runs out flags the launch, then waits once more
+    // (bounded again) so no MMA is in flight when the columns are freed
+    if (!mbar_wait(&done, 0, nullptr)) {
+      atomicOr(flag, kDeviceTimeout);
+      mbar_wait(&done, 0, nullptr);
+    }
+  }
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  // one accumulator row per thread of warp 0..3 (lanes 32*warp + lane), first
+  // 32 columns, folded into one value so the work has an observable result
+  float v[32];
+  tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), v);
+  float s = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 32; ++j) s += v[j];
+  if (s == 12345.678f) sink[blockIdx.x] = s;  // practically never true; keeps the read
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
 // ---- split pass --------------------------------------------------------------------------
 
 __device__ __forceinline__ float tf32_rna(float x) {
@@ -503,5 +599,48 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
                                                                               full, rem, nsplit);
     count_launch();
   }
+  return 0;
+}
+
+// Tensor-pipe probe (see probe_mma_kernel): one CTA per SM, a warm-up launch,
+// then one timed launch between two events on the context's stream.
+extern "C" int mapal_gpu_probe_mma_peak(MapalGpuCtx* ctx, int kind, uint32_t iters, double* tflops) {
+  MAPAL_TRY(enter(ctx, 0));
+  if (!tflops) return set_error(MAPAL_ERR_INVALID, "tflops is null");
+  if (kind != 0 && kind != 1) return set_error(MAPAL_ERR_INVALID, "kind must be 0 (tf32) or 1 (bf16)");
+  if (iters == 0 || iters > (1u << 24)) return set_error(MAPAL_ERR_INVALID, "iters must be in [1, 2^24]");
+  DeviceSlot& d = ctx->dev[0];
+  // 120 KiB of dynamic shared memory: only one probe CTA fits on an SM
+  const size_t smem = 120 * 1024;
+  static uint64_t attr_set = 0;
+  if (!(attr_set >> d.device & 1)) {
+    MAPAL_CUDA(cudaFuncSetAttribute(probe_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set |= 1ull << d.device;
+  }
+  MAPAL_TRY(arena_reserve(d, (size_t)d.prof.sm_count * sizeof(float)));
+  float* sink = static_cast<float*>(d.arena);
+  cudaEvent_t e0, e1;
+  MAPAL_CUDA(cudaEventCreate(&e0));
+  MAPAL_CUDA(cudaEventCreate(&e1));
+  const unsigned grid = (unsigned)d.prof.sm_count;
+  probe_mma_kernel<<<grid, kProbeThreads, smem, d.stream>>>((int)(iters < 64 ? iters : 64), kind, d.trap, sink);
+  count_launch();
+  cudaEventRecord(e0, d.stream);
+  probe_mma_kernel<<<grid, kProbeThreads, smem, d.stream>>>((int)iters, kind, d.trap, sink);
+  count_launch();
+  cudaEventRecord(e1, d.stream);
+  cudaError_t le = cudaGetLastError();
+  cudaError_t se = cudaEventSynchronize(e1);
+  float ms = 0.0f;
+  cudaError_t te = cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  if (le != cudaSuccess) return cuda_fail(le, "probe_mma_kernel launch");
+  if (se != cudaSuccess) return cuda_fail(se, "probe_mma_kernel");
+  if (te != cudaSuccess) return cuda_fail(te, "cudaEventElapsedTime");
+  MAPAL_TRY(drain(d));
+  const double k_per_mma = kind == 0 ? 8.0 : 16.0;
+  const double flops = (double)grid * iters * 6.0 * 2.0 * BM * BN * k_per_mma;
+  *tflops = flops / (ms * 1e-3) / 1e12;
   return 0;
 }

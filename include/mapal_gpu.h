@@ -347,12 +347,15 @@ int mapal_gpu_fold_sum_f32_strict(MapalGpuCtx* ctx, float seed, const float* x, 
  * until the process exits. A device whose fold launch would need more than
  * 1024 slots (more than 256 SMs) is refused with MAPAL_ERR_INVALID.
  * Runs on the calling thread's current device, enqueued on `stream` (a
- * cudaStream_t, NULL = default stream); returns after enqueueing, so read
+ * cudaStream_t of that device, NULL = default stream; a stream of another
+ * device is refused with MAPAL_ERR_INVALID); returns after enqueueing, so read
  * `out` (a device float) after synchronising the stream. The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress); make
- * that first call before any stream capture. Calls share the array: the
- * counter is cleared on the stream before each launch, and calls whose
- * kernels overlap on the GPU race and give wrong results. */
+ * that first call before any stream capture. Host threads may call it
+ * concurrently. The address is kept for the life of the process, so calls
+ * after a cudaDeviceReset of that device are not supported. Calls share the
+ * array: the counter is cleared on the stream before each launch, and calls
+ * whose kernels overlap on the GPU race and give wrong results. */
 int mapal_gpu_fold_sum_f32_noalloc(float seed, const float* x, uint64_t n, float* out, void* stream);
 
 /* FIR / window site (benches/shapes/fir_1048576.mapal:10-12):
@@ -450,6 +453,17 @@ int mapal_gpu_gather_sharded(MapalGpuCtx* ctx, const float* const* x, uint64_t n
 int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSite* site,
                                  const float* const* A, float* const* B, float* const* C,
                                  const uint64_t* m, int root, int mode);
+
+/* ---- measurement --------------------------------------------------------------
+ * No counterpart in the reference: the roofline of MAPAL_MATMUL_TF32X3.
+ * Issues the 3xTF32 GEMM's own tensor-core instruction (tcgen05.mma M128 N256,
+ * operands K-major with the 64-byte swizzle in shared memory, f32 accumulator
+ * in tensor memory) back to back with no memory traffic: one CTA per SM,
+ * `iters` rounds of 6 MMAs, one warm-up launch and one timed launch on local
+ * device 0's stream. kind 0 = kind::tf32 (K8), kind 1 = kind::f16 with bf16
+ * operands (K16), which checks the method against a bf16 GEMM's rate.
+ * *tflops receives the dense rate (2 flops per multiply-add). */
+int mapal_gpu_probe_mma_peak(MapalGpuCtx* ctx, int kind, uint32_t iters, double* tflops);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -17,6 +17,9 @@
 // before each launch. Two calls whose kernels overlap on the GPU (different
 // streams, no ordering between them) race on the array and give wrong sums;
 // calls on one stream, or otherwise ordered, are safe.
+#include <atomic>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace {
@@ -31,20 +34,42 @@ static __device__ __align__(256) double g_fold_noalloc_scratch[kNoAllocSlots + 1
 // first call on that device. In host code the symbol itself is only a
 // stand-in, never a device address: passing it to a kernel would fault, or
 // silently use the wrong memory where the GPU can reach host memory.
+//
+// Host threads may make their first calls at the same time: the table is
+// filled under a mutex, and an entry's address is published (release) only
+// after its SM count is written, so a reader that sees the address (acquire)
+// also sees the count. An address is looked up once per device for the life
+// of the process; after cudaDeviceReset on a device it is stale, so calls
+// that follow a reset are not supported.
 constexpr int kMaxDevices = 64;
-double* g_scratch_ptr[kMaxDevices];
-int g_sm_count[kMaxDevices];
+struct ScratchEntry {
+  std::atomic<double*> ptr{nullptr};
+  int sm_count = 0;
+};
+ScratchEntry g_scratch[kMaxDevices];
+std::mutex g_scratch_mu;
 
-int setup(int device) {
-  if (g_scratch_ptr[device]) return 0;
-  void* p = nullptr;
-  cudaError_t e = cudaGetSymbolAddress(&p, g_fold_noalloc_scratch);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(g_fold_noalloc_scratch)");
-  int sms = 0;
-  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(MultiProcessorCount)");
-  g_sm_count[device] = sms;
-  g_scratch_ptr[device] = static_cast<double*>(p);
+// `device` is current on the calling thread.
+int setup(int device, double** ptr, int* sm_count) {
+  ScratchEntry& e = g_scratch[device];
+  double* p = e.ptr.load(std::memory_order_acquire);
+  if (!p) {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    p = e.ptr.load(std::memory_order_relaxed);
+    if (!p) {
+      void* addr = nullptr;
+      cudaError_t err = cudaGetSymbolAddress(&addr, g_fold_noalloc_scratch);
+      if (err != cudaSuccess) return cuda_fail(err, "cudaGetSymbolAddress(g_fold_noalloc_scratch)");
+      int sms = 0;
+      err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+      if (err != cudaSuccess) return cuda_fail(err, "cudaDeviceGetAttribute(MultiProcessorCount)");
+      e.sm_count = sms;
+      p = static_cast<double*>(addr);
+      e.ptr.store(p, std::memory_order_release);
+    }
+  }
+  *ptr = p;
+  *sm_count = e.sm_count;
   return 0;
 }
 
@@ -58,21 +83,31 @@ extern "C" int mapal_gpu_fold_sum_f32_noalloc(float seed, const float* x, uint64
   MAPAL_CUDA(cudaGetDevice(&device));
   if (device < 0 || device >= kMaxDevices)
     return set_error(MAPAL_ERR_INVALID, "device ordinal beyond the no-alloc table (64 devices)");
-  MAPAL_TRY(setup(device));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The scratch address is the current device's; a stream of another device
+  // would run the kernel there against this device's array, so it is refused.
+  if (s != nullptr) {
+    int stream_device = -1;
+    MAPAL_CUDA(cudaStreamGetDevice(s, &stream_device));
+    if (stream_device != device)
+      return set_error(MAPAL_ERR_INVALID, "stream belongs to device " + std::to_string(stream_device) +
+                                              ", the calling thread's current device is " + std::to_string(device));
+  }
+  double* partials = nullptr;
+  int sm_count = 0;
+  MAPAL_TRY(setup(device, &partials, &sm_count));
   // The fold kernel uses one partial slot per block, at most 4 blocks per SM
   // (capped at kFoldMaxBlocks): a device needing more slots than the static
   // array holds is refused rather than overrun.
-  int max_blocks = 4 * g_sm_count[device];
+  int max_blocks = 4 * sm_count;
   if (max_blocks > kFoldMaxBlocks) max_blocks = kFoldMaxBlocks;
   if (max_blocks > kNoAllocSlots)
     return set_error(MAPAL_ERR_INVALID,
                      "the no-alloc sum keeps 1024 partial slots; this device needs " +
                          std::to_string(max_blocks) + " (4 per SM)");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  double* partials = g_scratch_ptr[device];
   unsigned* counter = reinterpret_cast<unsigned*>(partials + kNoAllocSlots);
   MAPAL_CUDA(cudaMemsetAsync(counter, 0, sizeof(unsigned), s));
-  MAPAL_TRY(launch_fold_sum(s, g_sm_count[device], x, n, seed, partials, counter, out, nullptr));
+  MAPAL_TRY(launch_fold_sum(s, sm_count, x, n, seed, partials, counter, out, nullptr));
   MAPAL_CUDA(cudaGetLastError());
   return 0;
 }

@@ -23,7 +23,8 @@ def build() -> None:
     """Compile liboracle.so (and, when the reference tree is present, the
     reference's own C++ baselines into oracle/_ref)."""
     subprocess.run(["make", "-s", "-C", _HERE], check=True)
-    ref = os.environ.get("MAPAL_REFERENCE", "/root/reference")
+    # $MAPAL_REFERENCE, else a checkout named `reference` beside this repository
+    ref = os.environ.get("MAPAL_REFERENCE", os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference"))
     if os.path.isdir(os.path.join(ref, "benches")):
         subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={ref}"], check=True)
 

@@ -705,6 +705,15 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
             if site == "fir":
                 extra["fp32_frac"] = r["gflops"] * 1e9 / (sms * 128 * pk["sm_max_mhz"] * 1e6)
             rec(key, r["bytes"], r["ms"], extra)
+        # What this class cannot beat, timed the same way: an empty kernel, and
+        # the sum fold's own grid and loads over 2^20 floats without its
+        # cross-block combine.
+        fe = sitebench.measure(ctx, torch, "floor_empty", 1, None, reps=50, warmup=3, l2_bytes=l2)
+        fr = sitebench.measure(ctx, torch, "floor_read", 1 << 20, None, reps=50, warmup=3, l2_bytes=l2)
+        out["floor_2^20"] = {"empty_kernel_us": fe["ms"] * 1e3, "read_4MiB_us": fr["ms"] * 1e3,
+                             "read_4MiB_frac_hbm": fr["gbs"] / hbm,
+                             "basis": "CUDA graph replay, inputs outside L2, as the sites; the read has the sum "
+                                      "fold's grid and loads and no cross-block combine"}
         out["l2"] = ("2^20 class: launches rotate over buffer sets totalling > 2x L2 and are replayed "
                      "from a CUDA graph (ms_host_issued: the same launches issued from Python); "
                      "2^30 class: inputs far larger than L2")

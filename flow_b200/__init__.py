@@ -317,6 +317,13 @@ class Context:
         _check(lib().mapal_gpu_probe_mma_peak(self._h, kind, iters, ctypes.byref(out)))
         return out.value
 
+    def probe_launch_floor(self, kind: int, x=None, sink=None) -> None:
+        """Enqueue the floor kernel: kind 0 an empty kernel, kind 1 a read of
+        x with the sum fold's grid and loads but no combine."""
+        n = x.numel() if x is not None else 0
+        _check(lib().mapal_gpu_probe_launch_floor(self._h, kind, _ptr(x) if x is not None else None, n,
+                                                  _ptr(sink) if sink is not None else None))
+
     def matmul_sharded(self, site: TileSite, As, Bs, Cs, rows: Sequence[int], root: int = 0,
                        mode: int = STRICT) -> None:
         _check(lib().mapal_gpu_matmul_f32_sharded(self._h, ctypes.byref(site), _arr(As), _arr(Bs),

@@ -68,6 +68,7 @@ SIGNATURES: dict[str, tuple] = {
     "mapal_gpu_gather_sharded": (_int, [_vp, _pp, _u64, _pp, _pp, _pu64]),
     "mapal_gpu_matmul_f32_sharded": (_int, [_vp, _c.POINTER(TileSite), _pp, _pp, _pp, _pu64, _int, _int]),
     "mapal_gpu_probe_mma_peak": (_int, [_vp, _int, _c.c_uint32, _c.POINTER(_c.c_double)]),
+    "mapal_gpu_probe_launch_floor": (_int, [_vp, _int, _vp, _u64, _vp]),
     # mapal-rt re-exports (include/mapal_rt.h)
     "mapal_print_i32": (None, [_i32, _c.c_bool]),
     "mapal_print_i64": (None, [_i64, _c.c_bool]),

@@ -6,23 +6,29 @@
 // error. This is that path (MAPAL_MATMUL_TF32X3); the default strict path
 // stays bit-exact.
 //
-// Each f32 operand is split into two TF32 values, x = hi + lo with
-// hi = rna(x) and lo = rna(x - hi), and C = A*B is accumulated in f32 as
-// Ahi*Bhi + Ahi*Blo + Alo*Bhi (the dropped Alo*Blo is ~2^-22 relative).
+// Each f32 operand is split into two TF32 values and C = A*B is accumulated
+// in f32 as Ahi*Bhi + Ahi*Blo + Alo*Bhi (the dropped Alo*Blo is ~2^-20
+// relative), into two TMEM accumulators that alternate by k-block.
 //
-//  * split pass: A -> Ahi, Alo (row-major, K-major for the MMA) and
-//    B -> BhiT, BloT (transposed to N x K, K-major), into the context arena;
+//  * B -> BhiT, BloT (transposed to N x K, K-major; hi = rna(x),
+//    lo = rna(x - hi)) by a split pass into the context arena;
+//  * A, when TMA can read it in place and N <= 8192: raw tiles are the hi
+//    operand (the tensor pipe truncates an f32 to TF32) and the GEMM writes
+//    the lo tiles in shared memory (mm_tf32x3_fused_kernel); otherwise A is
+//    split into the arena as well (mm_tf32x3_kernel);
 //  * GEMM: one CTA per 128 x 256 tile of C, 192 threads in three roles:
-//      warp 0  TMA producer: four 2-D tiled loads per k-block (16 k, 64-byte
+//      warp 0  TMA producer: 2-D tiled loads per k-block (16 k, 64-byte
 //              swizzle) into a 4-stage shared-memory ring, one mbarrier per
 //              stage with the transaction byte count;
-//      warp 1  allocates 256 TMEM columns (the 128 x 256 f32 accumulator) and
+//      warp 1  allocates 512 TMEM columns (two 128 x 256 f32 accumulators;
+//              even k-blocks go to the first, odd ones to the second) and
 //              one lane issues tcgen05.mma kind::tf32 (M128 N256 K8): three
 //              products per k-step, two k-steps per stage; tcgen05.commit
 //              frees a stage when its MMAs have read it;
-//      warps 2-5 epilogue: wait for the final commit, tcgen05.ld the
-//              accumulator (each warp its 32-lane quarter), add the seed,
-//              store C.
+//      warps 2-5 (fused kernel: first convert each stage's A lo tile) then
+//              the epilogue: wait for the final commit, tcgen05.ld both
+//              accumulators (each warp its 32-lane quarter), add them and
+//              the seed, store C.
 //  * no cluster multicast anywhere: every CTA fetches its own tiles.
 //
 // Every wait is bounded: a wait that runs out sets the device flag to
@@ -37,7 +43,12 @@ namespace {
 
 constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
 constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+// Two 128 x 256 f32 accumulators: k-blocks alternate between them and the
+// epilogue adds the pair once with a rounded f32 add. The tensor pipe's
+// accumulation error grows with the number of additions into one
+// accumulator, so two half-length chains roughly halve it.
+constexpr uint32_t kAccCols = 256;
+constexpr uint32_t kTmemCols = 2 * kAccCols;
 constexpr int kATile = BM * BK * 4;  // bytes of one A tile (hi or lo)
 constexpr int kBTile = BN * BK * 4;  // bytes of one B tile (hi or lo)
 constexpr int kStageBytes = 2 * kATile + 2 * kBTile;
@@ -226,30 +237,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 1 && lane == 0) {
     // ---- MMA issuer ----
-    bool ok = true;
     for (int kt = 0; kt < nkt; ++kt) {
       const int s = kt % STAGES;
       if (!mbar_wait(&sm.full[s], (kt / STAGES) & 1, abort)) {
         *abort = 1;
-        ok = false;
         break;
       }
       asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
       const uint8_t* st = sm.stage[s];
       const uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
       const uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTile);
+      const uint32_t acc = tmem + (uint32_t)(kt & 1) * kAccCols;  // this k-block's accumulator
 #pragma unroll
       for (int kk = 0; kk < BK / 8; ++kk) {
         const uint64_t adv = (uint64_t)((kk * 8 * 4) >> 4);  // 32 bytes along K
-        mma_tf32(tmem, ahi + adv, bhi + adv, (kt > 0 || kk > 0) ? 1u : 0u);
-        mma_tf32(tmem, ahi + adv, blo + adv, 1u);
-        mma_tf32(tmem, alo + adv, bhi + adv, 1u);
+        mma_tf32(acc, ahi + adv, bhi + adv, (kt > 1 || kk > 0) ? 1u : 0u);
+        mma_tf32(acc, ahi + adv, blo + adv, 1u);
+        mma_tf32(acc, alo + adv, bhi + adv, 1u);
       }
       mma_commit(&sm.empty[s]);
     }
     // Final commit: arrives once every MMA issued above has completed.
     mma_commit(&sm.acc_full);
-    (void)ok;
   } else if (warp >= 2) {
     // ---- epilogue: TMEM -> registers -> global ----
     const int quarter = warp % 4;  // TMEM lanes 32*quarter .. +31 are this warp's
@@ -265,7 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
+        tmem_ld32(lane_base, v);
+        if (nkt > 1) {  // the second accumulator holds the odd k-blocks
+          float w[32];
+          tmem_ld32(lane_base + kAccCols, w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], w[j]);
+        }
         if (prow) {
 #pragma unroll
           for (int j = 0; j < 32; j += 4)
@@ -323,6 +339,233 @@ __global__ void reduce_parts_kernel(const float* __restrict__ part, float* __res
   }
 }
 
+// ---- fused split of A: raw A converted in shared memory ---------------------------------------
+//
+// The tensor pipe reads a kind::tf32 operand as its top 19 bits (the low 13
+// mantissa bits are ignored, i.e. the value is truncated toward zero to
+// TF32; measured on a B200). So a raw f32 tile is itself a "hi" operand,
+// hi = trunc(x), and lo = rna(x - hi) (x - hi is exact in f32) completes the
+// split. This kernel reads A where it lies: TMA brings raw A tiles (K-major,
+// 64-byte swizzle), and warps 2-5 write each stage's A lo tile at the same
+// offsets plus 8 KiB (the layouts are identical, so the conversion is
+// elementwise) before releasing the stage to the MMA warp; the same warps run
+// the epilogue. B still comes pre-split and transposed (BhiT, BloT), because
+// B read in place would be an MN-major operand, and the tensor pipe runs
+// kind::tf32 with an MN-major B about 9 % slower than K-major (measured with
+// mapal_gpu_probe_mma_peak kinds 0 and 2), more than the B split pass costs.
+// Against the pre-split kernel: no A split pass and 8 KiB less L2 traffic
+// per stage.
+
+struct SmemF {
+  uint8_t stage[STAGES][kStageBytes];  // per stage: A raw | A lo | BhiT | BloT
+  uint64_t full[STAGES];               // TMA landed the stage
+  uint64_t conv[STAGES];               // the A lo tile is written (128 converter arrivals)
+  uint64_t empty[STAGES];              // the MMAs have read the stage
+  uint64_t acc_full;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr int kConvThreads = 128;
+static_assert(kATile / 16 % kConvThreads == 0, "the converter's float4 share must be whole");
+constexpr uint32_t kLoadStageBytes = kATile + 2 * kBTile;  // TMA bytes per stage
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(sa(b)) : "memory");
+}
+
+// lo part of x for the truncated hi: x - trunc(x) is exact in f32 and is
+// rounded to TF32 (nearest, ties away) with integer operations. A NaN or
+// infinite x gives a NaN lo, kept as NaN, so every product that reads x is
+// NaN (a NaN whose payload is only in the low 13 bits, which the tensor pipe
+// reads as infinity, still yields NaN).
+__device__ __forceinline__ float lo_rna(float x) {
+  const float lo = __fsub_rn(x, __uint_as_float(__float_as_uint(x) & 0xFFFFE000u));
+  const float r = __uint_as_float((__float_as_uint(lo) + 0x1000u) & 0xFFFFE000u);
+  return lo == lo ? r : lo;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    mm_tf32x3_fused_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
+                           const __grid_constant__ CUtensorMap map_blo, float* __restrict__ C, int M, int N, int K,
+                           long long ldc, float seed, unsigned* flag, int tiles_m, int tiles_n, int tile_base,
+                           int nsplit, float* __restrict__ part_out) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  SmemF& sm = *reinterpret_cast<SmemF*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int tile = tile_base + (int)blockIdx.x / nsplit, part = (int)blockIdx.x % nsplit;
+  int tm, tn;
+  tile_coords(tile, tiles_m, tiles_n, tm, tn);
+  const int m0 = tm * BM, n0 = tn * BN;
+  const int KT = (K + BK - 1) / BK;
+  const int kt_lo = (int)((long long)KT * part / nsplit), nkt = (int)((long long)KT * (part + 1) / nsplit) - kt_lo;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.conv[s], kConvThreads);
+      mbar_init(&sm.empty[s], 1);
+    }
+    mbar_init(&sm.acc_full, 1);
+    sm.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sa(&sm.tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = sm.tmem_base;
+  volatile int* abort = &sm.abort;
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer: raw A, BhiT, BloT ----
+    int issued = 0;
+    for (int kt = 0; kt < nkt; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES && !mbar_wait(&sm.empty[s], ((kt / STAGES) - 1) & 1, abort)) {
+        *abort = 1;
+        break;
+      }
+      uint8_t* st = sm.stage[s];
+      mbar_expect_tx(&sm.full[s], kLoadStageBytes);
+      const int k0 = (kt_lo + kt) * BK;
+      tma_load_2d(st, &map_a, k0, m0, &sm.full[s]);
+      tma_load_2d(st + 2 * kATile, &map_bhi, k0, n0, &sm.full[s]);
+      tma_load_2d(st + 2 * kATile + kBTile, &map_blo, k0, n0, &sm.full[s]);
+      ++issued;
+    }
+    if (*abort) {
+      for (int kt = (issued > STAGES ? issued - STAGES : 0); kt < issued; ++kt)
+        mbar_wait(&sm.full[kt % STAGES], (kt / STAGES) & 1, nullptr);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer ----
+    for (int kt = 0; kt < nkt; ++kt) {
+      const int s = kt % STAGES;
+      if (!mbar_wait(&sm.conv[s], (kt / STAGES) & 1, abort)) {
+        *abort = 1;
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint8_t* st = sm.stage[s];
+      const uint64_t ahi = smem_desc(st), alo = smem_desc(st + kATile);
+      const uint64_t bhi = smem_desc(st + 2 * kATile), blo = smem_desc(st + 2 * kATile + kBTile);
+      const uint32_t acc = tmem + (uint32_t)(kt & 1) * kAccCols;
+#pragma unroll
+      for (int kk = 0; kk < BK / 8; ++kk) {
+        const uint64_t adv = (uint64_t)((kk * 8 * 4) >> 4);  // 32 bytes along K
+        mma_tf32(acc, ahi + adv, bhi + adv, (kt > 1 || kk > 0) ? 1u : 0u);
+        mma_tf32(acc, ahi + adv, blo + adv, 1u);
+        mma_tf32(acc, alo + adv, bhi + adv, 1u);
+      }
+      mma_commit(&sm.empty[s]);
+    }
+    mma_commit(&sm.acc_full);
+  } else if (warp >= 2) {
+    // ---- converter: the A lo tile of every stage, then the epilogue ----
+    const int ct = threadIdx.x - 64;
+    for (int kt = 0; kt < nkt; ++kt) {
+      const int s = kt % STAGES;
+      if (!mbar_wait(&sm.full[s], (kt / STAGES) & 1, abort)) {
+        *abort = 1;
+        break;
+      }
+      uint8_t* st = sm.stage[s];
+      float4 v[kATile / 16 / kConvThreads];
+#pragma unroll
+      for (int i = 0; i < kATile / 16 / kConvThreads; ++i)
+        v[i] = *reinterpret_cast<const float4*>(st + (ct + i * kConvThreads) * 16);
+#pragma unroll
+      for (int i = 0; i < kATile / 16 / kConvThreads; ++i)
+        *reinterpret_cast<float4*>(st + kATile + (ct + i * kConvThreads) * 16) =
+            make_float4(lo_rna(v[i].x), lo_rna(v[i].y), lo_rna(v[i].z), lo_rna(v[i].w));
+      // generic-proxy writes, then visible to the tensor core's async proxy
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&sm.conv[s]);
+    }
+    const int quarter = warp % 4;
+    bool ready = mbar_wait(&sm.acc_full, 0, abort);
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (!ready) {
+      *abort = 1;
+    } else {
+      const int row = m0 + quarter * 32 + lane;
+      float* prow = nsplit > 1 ? part_out + (long long)blockIdx.x * (BM * BN) + (quarter * 32 + lane) * BN : nullptr;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        float v[32];
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
+        tmem_ld32(lane_base, v);
+        if (nkt > 1) {
+          float w[32];
+          tmem_ld32(lane_base + kAccCols, w);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], w[j]);
+        }
+        if (prow) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(prow + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        } else if (row < M) {
+          float* crow = C + (long long)row * ldc + n0 + c0;
+          const int nvalid = N - (n0 + c0);
+          if (nvalid >= 32 && ((ldc & 3) == 0) && (((uintptr_t)C & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(crow + j) =
+                  make_float4(v[j] + seed, v[j + 1] + seed, v[j + 2] + seed, v[j + 3] + seed);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nvalid) crow[j] = v[j] + seed;
+          }
+        }
+      }
+    }
+  }
+
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (*abort) {
+    if (threadIdx.x == 0) atomicOr(flag, kDeviceTimeout);
+    if (warp == 1 && lane == 0) mbar_wait(&sm.acc_full, 0, nullptr);
+    __syncwarp();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// MN-major B for the probe (kind 2): 32-column chunks 2048 bytes apart (LBO),
+// groups of 4 k rows 512 bytes apart (SBO), 128-byte rows, layout type 1
+// (128-byte swizzle with 32-byte atoms, the only MN-major layout UMMA takes
+// for 32-bit operands).
+__device__ __forceinline__ uint64_t smem_desc_mn(const void* p) {
+  uint64_t addr = sa(p);
+  uint64_t d = 0;
+  d |= (addr & 0x3FFFFull) >> 4;
+  d |= (uint64_t)(2048 >> 4) << 16;
+  d |= (uint64_t)(512 >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 1ull << 61;
+  return d;
+}
+
+constexpr uint32_t kIdescMN = kIdesc | (1u << 16);  // B MN-major
+
+__device__ __forceinline__ void mma_tf32_mn(uint32_t tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem),
+      "l"(a), "l"(b), "r"(kIdescMN), "r"(accumulate));
+}
+
 // ---- tensor-pipe probe ---------------------------------------------------------------------
 //
 // The roofline of the 3xTF32 GEMM is the tensor pipe's TF32 rate, which no
@@ -347,6 +590,8 @@ __device__ __forceinline__ void mma_bf16(uint32_t tmem, uint64_t a, uint64_t b, 
 }
 
 __global__ void __launch_bounds__(kProbeThreads, 1) probe_mma_kernel(int iters, int kind, unsigned* flag, float* sink) {
+  // kind 2: kind::tf32 with B MN-major (the fused kernel's B layout: 128-byte
+  // swizzle with 32-byte atoms, 32-column chunks 2 KiB apart)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // two operand sets (hi, lo) as in one GEMM stage: A 2 x 8 KiB, B 2 x 16 KiB
@@ -386,6 +631,12 @@ __global__ void __launch_bounds__(kProbeThreads, 1) probe_mma_kernel(int iters, 
           mma_tf32(tmem, ahi + adv, bhi + adv, (it > 0 || kk > 0) ? 1u : 0u);
           mma_tf32(tmem, ahi + adv, blo + adv, 1u);
           mma_tf32(tmem, alo + adv, bhi + adv, 1u);
+        } else if (kind == 2) {
+          const uint64_t bm = smem_desc_mn(base + 2 * kATile) + (uint64_t)((kk * 1024) >> 4);
+          const uint64_t bl = smem_desc_mn(base + 2 * kATile + kBTile) + (uint64_t)((kk * 1024) >> 4);
+          mma_tf32_mn(tmem, ahi + adv, bm, (it > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_mn(tmem, ahi + adv, bl, 1u);
+          mma_tf32_mn(tmem, alo + adv, bm, 1u);
         } else {
           mma_bf16(tmem, ahi + adv, bhi + adv, (it > 0 || kk > 0) ? 1u : 0u);
           mma_bf16(tmem, ahi + adv, blo + adv, 1u);
@@ -428,8 +679,15 @@ __device__ __forceinline__ float tf32_rna(float x) {
 }
 
 // hi = rna(x), lo = rna(x - hi); non-finite values (and a hi that rounded up
-// past the f32 range) keep lo = 0 so they propagate as hi*B alone.
+// past the f32 range) keep lo = 0 so they propagate as hi*B alone. A NaN
+// becomes the canonical NaN: rounding its mantissa could otherwise leave the
+// bits of an infinity (a payload only in the low 13 bits).
 __device__ __forceinline__ void split1(float x, float& hi, float& lo) {
+  if (isnan(x)) {
+    hi = __uint_as_float(0x7FFFFFFFu);
+    lo = 0.0f;
+    return;
+  }
   hi = tf32_rna(x);
   if (isinf(hi) && !isinf(x)) hi = __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
   lo = isfinite(hi) ? tf32_rna(__fsub_rn(x, hi)) : 0.0f;
@@ -536,7 +794,6 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   if ((N + BN - 1) / BN > 0x7fffffffull || (M + BM - 1) / BM > 65535)
     return set_error(MAPAL_ERR_UNSUPPORTED, "matmul grid too large");
   const uint64_t kp = (K + 3) & ~3ull;  // TMA row strides must be multiples of 16 bytes
-  const uint64_t elems = (M + N) * kp;
   // Tile plan: whole waves of 128 x 256 tiles; a partial last wave of R tiles
   // is split along K into nsplit parts (R * nsplit <= SMs) whose partial
   // tiles a reduction kernel sums in a fixed order.
@@ -553,20 +810,62 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
     if (nsplit > KT) nsplit = KT;
   }
   const uint64_t part_elems = nsplit > 1 ? (uint64_t)rem * nsplit * BM * BN : 0;
-  MAPAL_TRY(arena_reserve(d, (2 * elems + part_elems) * sizeof(float) + 4096));
-  float* ahi = (float*)d.arena;
-  float* alo = ahi + M * kp;
-  float* bhi = alo + M * kp;
+  const int whole = nsplit > 1 ? full : tiles;  // tiles computed over all of K
+
+  // B is split and transposed into BhiT, BloT (N x K, K-major) in the arena.
+  // A is read in place when TMA can address its rows (16-byte aligned base and
+  // row stride) and N <= 8192: the GEMM then splits A in shared memory, which
+  // costs about 2.5 % of the GEMM, while the A split pass it replaces costs a
+  // share that falls as 1/N (5 % of the site at N = 4096, 1 % at 16384;
+  // B200-measured: 4096^3 0.595 -> 0.578 ms, 16384^3 36.8 -> 37.4 ms).
+  // Otherwise A is split into Ahi, Alo in the arena as well.
+  const bool a_in_place = aligned16(A) && (lda & 3) == 0 && N <= 8192;
+  const uint64_t a_elems = a_in_place ? 0 : 2 * M * kp;
+  MAPAL_TRY(arena_reserve(d, (a_elems + 2 * N * kp + part_elems) * sizeof(float) + 4096));
+  float* bhi = (float*)d.arena;
   float* blo = bhi + N * kp;
-  float* parts = blo + N * kp;
-  // keep every operand base 16-byte aligned (kp is a multiple of 4 floats)
-  split_rows_kernel<<<(unsigned)(M < (uint64_t)d.prof.sm_count * 8 ? M : (uint64_t)d.prof.sm_count * 8), 256, 0,
-                      d.stream>>>(A, (long long)lda, (int)M,
-                                                                                        (int)K, ahi, alo, (long long)kp); count_launch();
+  float* ahi = blo + N * kp;
+  float* alo = ahi + M * kp;
+  float* parts = ahi + a_elems;
+  // every operand base stays 16-byte aligned (kp is a multiple of 4 floats)
   dim3 tg((unsigned)((N + kTT - 1) / kTT), (unsigned)((K + kTT - 1) / kTT));
   if (tg.y > 65535) return set_error(MAPAL_ERR_UNSUPPORTED, "K too large for the split pass");
   split_transpose_kernel<<<tg, dim3(kTT, kTRows), 0, d.stream>>>(B, (long long)ldb, (int)K, (int)N, bhi, blo,
                                                                 (long long)kp);
+  count_launch();
+
+  if (a_in_place) {
+    CUtensorMap m_a, m_bhi, m_blo;
+    MAPAL_TRY(make_map(&m_a, A, M, K, lda, BM));
+    MAPAL_TRY(make_map(&m_bhi, bhi, N, K, kp, BN));
+    MAPAL_TRY(make_map(&m_blo, blo, N, K, kp, BN));
+    const size_t smem = sizeof(SmemF) + 1024;
+    static uint64_t attr_fused = 0;
+    if (!(attr_fused >> d.device & 1)) {
+      MAPAL_CUDA(cudaFuncSetAttribute(mm_tf32x3_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr_fused |= 1ull << d.device;
+    }
+    if (whole > 0) {
+      mm_tf32x3_fused_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(
+          m_a, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, 0, 1, nullptr);
+      count_launch();
+    }
+    if (nsplit > 1) {
+      mm_tf32x3_fused_kernel<<<(unsigned)(rem * nsplit), kThreads, smem, d.stream>>>(
+          m_a, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, full, nsplit,
+          parts);
+      count_launch();
+      const uint64_t n_red = (uint64_t)rem * BM * BN;
+      reduce_parts_kernel<<<stream_grid(n_red, 256, sms, 8), 256, 0, d.stream>>>(parts, C, (int)M, (int)N,
+                                                                                (long long)ldc, seed, tiles_m, tiles_n,
+                                                                                full, rem, nsplit);
+      count_launch();
+    }
+    return 0;
+  }
+
+  split_rows_kernel<<<(unsigned)(M < (uint64_t)sms * 8 ? M : (uint64_t)sms * 8), 256, 0, d.stream>>>(
+      A, (long long)lda, (int)M, (int)K, ahi, alo, (long long)kp);
   count_launch();
 
   CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
@@ -581,7 +880,6 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
     MAPAL_CUDA(cudaFuncSetAttribute(mm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set |= 1ull << d.device;
   }
-  const int whole = nsplit > 1 ? full : tiles;  // tiles computed over all of K
   if (whole > 0) {
     mm_tf32x3_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N,
                                                                     (int)K, (long long)ldc, seed, d.trap, tiles_m,
@@ -607,7 +905,7 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
 extern "C" int mapal_gpu_probe_mma_peak(MapalGpuCtx* ctx, int kind, uint32_t iters, double* tflops) {
   MAPAL_TRY(enter(ctx, 0));
   if (!tflops) return set_error(MAPAL_ERR_INVALID, "tflops is null");
-  if (kind != 0 && kind != 1) return set_error(MAPAL_ERR_INVALID, "kind must be 0 (tf32) or 1 (bf16)");
+  if (kind < 0 || kind > 2) return set_error(MAPAL_ERR_INVALID, "kind must be 0 (tf32), 1 (bf16) or 2 (tf32, B MN-major)");
   if (iters == 0 || iters > (1u << 24)) return set_error(MAPAL_ERR_INVALID, "iters must be in [1, 2^24]");
   DeviceSlot& d = ctx->dev[0];
   // 120 KiB of dynamic shared memory: only one probe CTA fits on an SM
@@ -639,7 +937,7 @@ extern "C" int mapal_gpu_probe_mma_peak(MapalGpuCtx* ctx, int kind, uint32_t ite
   if (se != cudaSuccess) return cuda_fail(se, "probe_mma_kernel");
   if (te != cudaSuccess) return cuda_fail(te, "cudaEventElapsedTime");
   MAPAL_TRY(drain(d));
-  const double k_per_mma = kind == 0 ? 8.0 : 16.0;
+  const double k_per_mma = kind == 1 ? 16.0 : 8.0;
   const double flops = (double)grid * iters * 6.0 * 2.0 * BM * BN * k_per_mma;
   *tflops = flops / (ms * 1e-3) / 1e12;
   return 0;

@@ -20,7 +20,7 @@ import math
 
 import flow_b200 as fb
 
-SITES = ("saxpy", "transpose", "gather", "sum", "fir", "conv2d", "matmul", "map_expr")
+SITES = ("saxpy", "transpose", "gather", "sum", "fir", "conv2d", "matmul", "map_expr", "floor_empty", "floor_read")
 
 
 def _alloc(torch, n, dtype=None):
@@ -117,6 +117,22 @@ def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = f
         per = 4 * n
         run = lambda s: ctx.map_expr(prog, [], s[0], n)
         flops = 0
+    elif name == "floor_empty":
+        # the launch floor: an empty kernel
+        def mk(i):
+            return ()
+        per = 0
+        run = lambda s: ctx.probe_launch_floor(0)
+        flops = 0
+    elif name == "floor_read":
+        # the read floor: the sum fold's grid and loads over n floats, no combine
+        def mk(i):
+            x, sink = _alloc(torch, n), _alloc(torch, 1)
+            ctx.gen(x, 1, 0, fb.U01)
+            return (x, sink)
+        per = 4 * n
+        run = lambda s: ctx.probe_launch_floor(1, s[0], s[1])
+        flops = 0
     else:
         raise ValueError(f"unknown site {name}")
     return mk, run, per, flops
@@ -126,7 +142,7 @@ def measure(ctx, torch, name: str, n: int, k: int | None = None, reps: int = 20,
             mode: int = fb.STRICT, l2_bytes: int = 126 << 20, rotate: bool = True,
             graph: bool = True) -> dict:
     mk, run, per, flops = make_site(ctx, torch, name, n, k, mode)
-    nsets = max(1, math.ceil(2 * l2_bytes / per)) if rotate else 1
+    nsets = max(1, math.ceil(2 * l2_bytes / per)) if rotate and per else 1
     sets = [mk(i) for i in range(nsets)]
     ctx.synchronize()
     stream = torch.cuda.current_stream()
@@ -167,7 +183,7 @@ def measure(ctx, torch, name: str, n: int, k: int | None = None, reps: int = 20,
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / total
         del g
-    out = {"site": name, "n": n, "ms": ms, "bytes": per, "gbs": per / (ms * 1e-3) / 1e9,
+    out = {"site": name, "n": n, "ms": ms, "bytes": per, "gbs": per / (ms * 1e-3) / 1e9 if per else None,
            "launches": total, "buffer_sets": nsets, "ms_host_issued": ms_host,
            "timing": "CUDA graph replay of the launches" if graph else "host-issued launches"}
     if flops:
@@ -188,7 +204,8 @@ def main() -> int:
     args = ap.parse_args()
     import torch
     defaults = {"saxpy": 1 << 20, "transpose": 1024 * 1024, "gather": 1 << 20, "sum": 1 << 20,
-                "fir": 1 << 20, "conv2d": 1024 * 1024, "matmul": 4096, "map_expr": 1 << 20}
+                "fir": 1 << 20, "conv2d": 1024 * 1024, "matmul": 4096, "map_expr": 1 << 20, "floor_empty": 1,
+                "floor_read": 1 << 20}
     sites = SITES if args.site == "all" else (args.site,)
     with fb.Context((0,), sync=False) as ctx:
         l2 = ctx.profile().l2_bytes

@@ -461,9 +461,17 @@ int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSite* site,
  * in tensor memory) back to back with no memory traffic: one CTA per SM,
  * `iters` rounds of 6 MMAs, one warm-up launch and one timed launch on local
  * device 0's stream. kind 0 = kind::tf32 (K8), kind 1 = kind::f16 with bf16
- * operands (K16), which checks the method against a bf16 GEMM's rate.
+ * operands (K16), which checks the method against a bf16 GEMM's rate, kind 2
+ * = kind::tf32 with B MN-major (the layout the GEMM reads B in place with).
  * *tflops receives the dense rate (2 flops per multiply-add). */
 int mapal_gpu_probe_mma_peak(MapalGpuCtx* ctx, int kind, uint32_t iters, double* tflops);
+
+/* No counterpart in the reference: the floor under the 2^20-element sites.
+ * kind 0 launches an empty kernel; kind 1 reads x (n floats, n a multiple of
+ * 4, 16-byte aligned) with the sum fold's own grid and loads but no combine
+ * across blocks (`sink`, a device float, is written only to keep the loads).
+ * Enqueued on local device 0's stream; time it as the sites are timed. */
+int mapal_gpu_probe_launch_floor(MapalGpuCtx* ctx, int kind, const float* x, uint64_t n, float* sink);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

@@ -1,10 +1,17 @@
 """The opt-in 3xTF32 tensor-core matmul (tcgen05) against the oracle.
 
-Tolerance (stated in the ABI header): for every cell
-    |C - C_oracle| <= 1e-5 * ||A[i, :]|| * ||B[:, j]||
-The split drops only Alo*Blo (about 2^-22 relative per product), so the
-observed error is orders of magnitude below the bound; integer-valued inputs
-(the reference's own generators) are exact."""
+Tolerance (stated in the ABI header): for every cell, with K <= 4096,
+    |C - A.B| <= TOL * ||A[i, :]|| * ||B[:, j]||,   TOL = 2e-6,
+A.B being the exact (f64) product. Why this bound: the split x = hi + lo
+(hi, lo TF32) makes each product exact to about 2^-21 relative; what remains
+is the tensor pipe's f32 accumulation, whose error grows with the number of
+additions into one accumulator (two alternating accumulators halve it).
+Measured on a B200: at most 7e-7 at K = 4096 and 3e-7 at K <= 1024, against
+1.3e-7 - 2.6e-7 for the strict f32 fold. A 3xTF32 that lost one cross
+product (2xTF32) errs by 1.4e-5 or more on these inputs and 1xTF32 by
+1.8e-5 or more: both fail the bound (test_tf32x3_tolerance_rejects_fewer_products,
+a numpy emulation on the same inputs). Integer-valued inputs (the
+reference's own generators) are exact."""
 import json
 import os
 
@@ -19,7 +26,9 @@ from _gpu import dev, empty_f32, host
 pytestmark = pytest.mark.gpu
 
 GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_outputs.json")))
-TOL = 1e-5
+TOL = 2e-6
+SHAPES = [(128, 256, 16), (256, 256, 256), (200, 300, 100), (129, 257, 33), (64, 64, 30), (1, 1, 1),
+          (1024, 1024, 1024), (300, 700, 4096)]
 
 
 @pytest.fixture(scope="module")
@@ -30,6 +39,7 @@ def ctx():
 
 
 def rel_err(C, want, A, B, M, N, K, rows=None):
+    """max |C - want| / (||A_i|| ||B_j||) over the cells of C."""
     A2 = A.reshape(M, K).astype(np.float64)
     B2 = B.reshape(K, N).astype(np.float64)
     rn = np.sqrt((A2 * A2).sum(1))
@@ -40,17 +50,28 @@ def rel_err(C, want, A, B, M, N, K, rows=None):
     return float(np.max(np.abs(C.astype(np.float64) - want.astype(np.float64)) / scale))
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 16), (256, 256, 256), (200, 300, 100), (129, 257, 33),
-                                   (64, 64, 30), (1, 1, 1), (1024, 1024, 1024), (300, 700, 4096)])
+def exact(A, B, M, N, K):
+    return A.reshape(M, K).astype(np.float64) @ B.reshape(K, N).astype(np.float64)
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
 def test_tf32x3_random(ctx, M, N, K):
     A = o.gen(M * K, 0, 0)
     B = o.gen(K * N, 0, M * K)
     C = empty_f32(M * N)
     ctx.matmul(fb.matmul_site(M, N, K), dev(A), dev(B), C, mode=fb.TF32X3)
     got = host(C).reshape(M, N)
-    want = o.matmul(A, B, M, N, K, threads=8).reshape(M, N)
     assert np.all(np.isfinite(got))
-    assert rel_err(got, want, A, B, M, N, K) <= TOL
+    ref = exact(A, B, M, N, K)
+    err = rel_err(got, ref, A, B, M, N, K)
+    # the strict fold's own error on the same inputs, for scale
+    strict = o.matmul(A, B, M, N, K, threads=8).reshape(M, N)
+    err_strict = rel_err(strict, ref, A, B, M, N, K)
+    print(f"3xTF32 {M}x{N}x{K}: max normalised error {err:.3g} (strict f32 fold {err_strict:.3g})")
+    assert err <= TOL
+    # within a small multiple of the strict fold's error (floor: one split
+    # product alone may err by 2^-21 relative)
+    assert err <= 4.0 * max(err_strict, 2.5e-7)
 
 
 def test_tf32x3_4096_sampled_rows(ctx):
@@ -60,9 +81,12 @@ def test_tf32x3_4096_sampled_rows(ctx):
     C = empty_f32(n * n)
     ctx.matmul(fb.matmul_site(n, n, n), dev(A), dev(B), C, mode=fb.TF32X3)
     c = host(C).reshape(n, n)
+    B2 = B.reshape(n, n).astype(np.float64)
     for r0 in (0, 2049, 4088):
-        want = o.matmul(A, B, n, n, n, row0=r0, row1=r0 + 8, threads=8).reshape(n, n)[r0:r0 + 8]
-        assert rel_err(c[r0:r0 + 8], want, A, B, n, n, n, rows=slice(r0, r0 + 8)) <= TOL
+        want = A.reshape(n, n)[r0:r0 + 8].astype(np.float64) @ B2
+        err = rel_err(c[r0:r0 + 8], want, A, B, n, n, n, rows=slice(r0, r0 + 8))
+        print(f"3xTF32 4096^3 rows {r0}..{r0 + 7}: max normalised error {err:.3g}")
+        assert err <= TOL
 
 
 @pytest.mark.parametrize("case", [c for c in GOLD["matmul_known_answers"] if c["n"] in (16, 256, 1024)],
@@ -90,7 +114,10 @@ def test_tf32x3_seed_and_padded_strides(ctx):
     assert rc == 0
     Ad = A.reshape(M, lda)[:, :K].ravel().copy()
     Bd = B.reshape(K, ldb)[:, :N].ravel().copy()
-    assert rel_err(host(C).reshape(M, N) - 3.0, want.reshape(M, N) - 3.0, Ad, Bd, M, N, K) <= TOL
+    # the seed is added after the product: compare C - seed with A.B
+    assert rel_err(host(C).reshape(M, N).astype(np.float64) - 3.0, exact(Ad, Bd, M, N, K),
+                   Ad, Bd, M, N, K) <= TOL
+    assert rc == 0 and want.size == M * N
 
 
 def test_tf32x3_repeatable(ctx):
@@ -100,3 +127,32 @@ def test_tf32x3_repeatable(ctx):
     ctx.matmul(fb.matmul_site(M, N, K), A, B, C1, mode=fb.TF32X3)
     ctx.matmul(fb.matmul_site(M, N, K), A, B, C2, mode=fb.TF32X3)
     assert torch.equal(C1, C2)
+
+
+@pytest.mark.parametrize("lda_pad", [0, 3])
+def test_tf32x3_non_finite_inputs(ctx, lda_pad):
+    # NaN propagates to every cell it touches, including a NaN whose payload
+    # lies only in the low 13 mantissa bits (the tensor pipe would read it as
+    # infinity after truncation); a cell touching an infinity is not finite.
+    # lda_pad = 3 takes the pre-split path (rows TMA cannot address in place).
+    M, N, K = 130, 260, 40
+    lda = K + lda_pad
+    A = o.gen(M * lda, 7, 0).reshape(M, lda)
+    B = o.gen(K * N, 7, M * lda).reshape(K, N)
+    A[3, 5] = np.float32(np.inf)
+    A[70, 11] = np.uint32(0x7F800001).view(np.float32)  # NaN, payload in the low bits only
+    B[9, 200] = np.float32(np.nan)
+    s = fb.matmul_site(M, N, K, lda=lda)
+    C = empty_f32(M * N)
+    ctx.matmul(s, dev(A.ravel()), dev(B.ravel()), C, mode=fb.TF32X3)
+    c = host(C).reshape(M, N)
+    assert np.all(np.isnan(c[70, :]))
+    assert np.all(np.isnan(c[:, 200]))
+    assert not np.any(np.isfinite(c[3, :]))
+    finite_rows = [r for r in range(M) if r not in (3, 70)]
+    cols = [j for j in range(N) if j != 200]
+    got = c[np.ix_(finite_rows, cols)]
+    Ad = A[finite_rows, :K]
+    Bd = B[:, cols]
+    assert rel_err(got, Ad.astype(np.float64) @ Bd.astype(np.float64), Ad.ravel(), Bd.ravel(),
+                   len(finite_rows), len(cols), K) <= TOL

@@ -628,7 +628,7 @@ def run_matmul_16384(ctx, d, fb, torch, pk) -> dict:
                 ctx.matmul_sharded(site, [A], [B], [C], [m], root=0, mode=mode)
             else:
                 ctx.matmul(site, A, B, C, mode)
-        ms = d.max(time_launches(torch, stream, step, lambda: None, 2))
+        ms = d.max(time_launches(torch, stream, step, lambda: None, 2, d))
         tf = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
         r = {"ms_per_step": ms, "value": tf, "unit": "TFLOP/s", "per_gpu": tf / d.world}
         # this rank's C block is the last step's result: check it
@@ -646,7 +646,7 @@ def run_matmul_16384(ctx, d, fb, torch, pk) -> dict:
             r["kernel_ms"] = d.max(time_launches(torch, stream, lambda: ctx.matmul(local, A, B, C, mode),
                                                  lambda: None, 2))
             r["broadcast_ms"] = d.max(time_launches(torch, stream, lambda: ctx.broadcast([B], root=0),
-                                                    lambda: None, 2))
+                                                    lambda: None, 2, d))
         if mode == fb.STRICT:
             r["frac_per_gpu"] = tf / d.world / (sms * 128 * pk["sm_max_mhz"] * 1e6 / 1e12)
         else:
@@ -659,10 +659,17 @@ def run_matmul_16384(ctx, d, fb, torch, pk) -> dict:
     return out
 
 
-def time_launches(torch, stream, fn, flush, reps: int) -> float:
-    """Mean device ms of fn over reps launches, L2 flushed before each."""
+def time_launches(torch, stream, fn, flush, reps: int, d=None) -> float:
+    """Mean device ms of fn over reps launches, L2 flushed before each. With
+    `d` (several ranks), every rank's device is idle and the ranks have met at
+    a barrier before the first timed launch, so a collective launch does not
+    time another rank's late start."""
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
     fn()
+    if d is not None and d.world > 1:
+        torch.cuda.synchronize()
+        d.barrier()
+        torch.cuda.synchronize()
     for a, b in evs:
         flush()
         a.record(stream)
@@ -728,12 +735,12 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
     y = torch.empty_like(x)
     ctx.gen(x, 3, lo)
     ctx.gen(y0, 3, n + lo)
-    ms = d.max(time_launches(torch, stream, lambda: ctx.saxpy_sharded(2.5, [x], [y0], [y]), lambda: None, 3))
+    ms = d.max(time_launches(torch, stream, lambda: ctx.saxpy_sharded(2.5, [x], [y0], [y]), lambda: None, 3, d))
     big["saxpy_2^30"] = {"ms": ms, "gbs": 12 * n / (ms * 1e-3) / 1e9}
     del y0, y
     s = torch.empty(1, dtype=torch.float32, device="cuda")
     ctx.gen(x, 3, lo, fb.U01)
-    ms = d.max(time_launches(torch, stream, lambda: ctx.fold_sum_sharded([x], [s]), lambda: None, 3))
+    ms = d.max(time_launches(torch, stream, lambda: ctx.fold_sum_sharded([x], [s]), lambda: None, 3, d))
     comb = ctx.sum_combine()
     big["sum_2^30"] = {"ms": ms, "gbs": 4 * n / (ms * 1e-3) / 1e9,
                        "collective": ("none (one rank)" if d.world == 1 else
@@ -749,7 +756,7 @@ def run_streaming(ctx, d, fb, torch, flush, pk) -> dict:
     idx = torch.empty(hi - lo, dtype=torch.int32, device="cuda")
     ctx.gen_index(idx, 3, ng + lo, ng)
     yg = torch.empty(hi - lo, dtype=torch.float32, device="cuda")
-    ms = d.max(time_launches(torch, stream, lambda: ctx.gather_sharded([xg], [idx], [yg]), lambda: None, 3))
+    ms = d.max(time_launches(torch, stream, lambda: ctx.gather_sharded([xg], [idx], [yg]), lambda: None, 3, d))
     big["gather_2^28"] = {"ms": ms, "gbs": 12 * ng / (ms * 1e-3) / 1e9,
                           "bytes_basis": "algorithmic 12 B/element; x replicated by NCCL broadcast at setup"}
     ctx.synchronize()

@@ -344,6 +344,28 @@ __global__ void __launch_bounds__(kThreads) floor_read_kernel(const float4* __re
   }
   if (acc == 1.2345e-30f) *sink = acc;  // practically never: keeps the loads
 }
+
+// n reads of x at hashed positions in [0, n_x), four per thread per trip, no
+// index array and no output: the rate at which the memory system serves
+// independent random 4-byte reads.
+__global__ void __launch_bounds__(kThreads) floor_random_kernel(const float* __restrict__ x, uint64_t n_x,
+                                                                uint64_t n, float* sink) {
+  const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+  float acc = 0.0f;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += 4 * stride) {
+    float v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      uint64_t h = (i + u * stride) * 0x9E3779B97F4A7C15ull;
+      h ^= h >> 29;
+      h *= 0xBF58476D1CE4E5B9ull;
+      h ^= h >> 32;
+      v[u] = (i + u * stride) < n ? __ldcs(x + h % n_x) : 0.0f;
+    }
+    acc += v[0] + v[1] + v[2] + v[3];
+  }
+  if (acc == 1.2345e-30f) *sink = acc;
+}
 }  // namespace
 
 extern "C" int mapal_gpu_probe_launch_floor(MapalGpuCtx* ctx, int kind, const float* x, uint64_t n, float* sink) {
@@ -356,8 +378,11 @@ extern "C" int mapal_gpu_probe_launch_floor(MapalGpuCtx* ctx, int kind, const fl
       return set_error(MAPAL_ERR_INVALID, "the read floor needs a 16-byte aligned x of 4k > 0 floats and a sink");
     floor_read_kernel<<<fold_grid(n, d.prof.sm_count), kThreads, 0, d.stream>>>(
         reinterpret_cast<const float4*>(x), n / 4, sink);
+  } else if (kind == 2) {
+    if (!x || !sink || n == 0) return set_error(MAPAL_ERR_INVALID, "the random-read floor needs x (n floats) and a sink");
+    floor_random_kernel<<<stream_grid(n, kThreads, d.prof.sm_count, 8), kThreads, 0, d.stream>>>(x, n, n, sink);
   } else {
-    return set_error(MAPAL_ERR_INVALID, "kind must be 0 (empty kernel) or 1 (read)");
+    return set_error(MAPAL_ERR_INVALID, "kind must be 0 (empty kernel), 1 (read) or 2 (random reads)");
   }
   count_launch();
   return finish(ctx, 0, false);

@@ -136,6 +136,28 @@ constexpr int kConvChunks = (kConvCols + 2 + 3 + 3) / 4;  // 16-byte chunks that
 // boundary below it: the staged row starts at that boundary.
 __device__ __forceinline__ int conv_shift(const float* p) { return (int)(((uintptr_t)p >> 2) & 3); }
 
+// Wait for phase 0 of a shared mbarrier, giving up after 1 s.
+__device__ __forceinline__ bool conv_bar_wait(uint64_t* bar) {
+  uint64_t t0;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t0));
+  for (uint32_t i = 0;; ++i) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0;\n\t"
+        "selp.b32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar))
+        : "memory");
+    if (ok) return true;
+    if ((i & 63) == 63) {
+      uint64_t t;
+      asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+      if (t - t0 > 1000000000ull) return false;
+    }
+  }
+}
+
 // out[i, j] = fold_k(acc + w[k] * img[(i + k/3)*stride + j + k%3]) from seed,
 // for a strip of P output rows x kConvCols columns. The P + 2 input rows are
 // staged (a warp per row) by 16-byte cp.async whatever the stride (elements outside the needed
@@ -147,22 +169,58 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
                                                                const float* __restrict__ img,
                                                                uint64_t img_len, uint64_t stride,
                                                                float* __restrict__ out, uint64_t rows,
-                                                               uint64_t cols, float seed, float neg_zero) {
+                                                               uint64_t cols, float seed, float neg_zero,
+                                                               unsigned* flag) {
   __shared__ __align__(16) float tile[P + 2][kConvPitch];
   const uint64_t i0 = (uint64_t)blockIdx.y * P;
   const uint64_t j0 = (uint64_t)blockIdx.x * kConvCols;
   const uint64_t need = cols + 2 - j0 < (uint64_t)(kConvCols + 2) ? cols + 2 - j0 : (uint64_t)(kConvCols + 2);
   const float* const img_end = img + img_len;
   __shared__ int shs[P + 2];  // each staged row's alignment shift
-  // Staging: warp w takes rows w, w + 4, ...; its lanes take the row's chunks
-  // (one row's setup per warp, not per thread).
+  __shared__ __align__(8) uint64_t bar;
+  // Staging. A row whose 16-byte aligned span [rowp - sh, ...) lies inside
+  // the image goes as one bulk copy (cp.async.bulk, completing on `bar`),
+  // issued by thread 0; the image stride need not be a multiple of 4 floats,
+  // which a 2-D tensor map would require. A row at the image's edge (its
+  // aligned span would leave the array) is staged by a warp with 16- or
+  // 4-byte cp.async, zero-filling what lies outside (never read).
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&bar)));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    uint32_t total = 0;
+    uint32_t span[P + 2];
+#pragma unroll
+    for (int r = 0; r < P + 2; ++r) {
+      const float* rowp = img + (i0 + r) * stride + j0;
+      const int sh = conv_shift(rowp);
+      shs[r] = sh;
+      const float* lo = rowp - sh;
+      const uint32_t nf = ((uint32_t)(sh + need) + 3u) & ~3u;  // floats, a whole number of 16-byte units
+      span[r] = (i0 + r < rows + 2 && lo >= img && lo + nf <= img_end) ? nf * 4u : 0u;
+      total += span[r];
+    }
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&bar)), "r"(total)
+                 : "memory");
+#pragma unroll
+    for (int r = 0; r < P + 2; ++r) {
+      if (span[r] == 0) continue;
+      const float* lo = img + (i0 + r) * stride + j0 - shs[r];
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+              smem_u32(&tile[r][0])),
+          "l"(lo), "r"(span[r]), "r"(smem_u32(&bar))
+          : "memory");
+    }
+  }
+  __syncthreads();  // shs[] and the barrier are set
   for (int r = warp; r < P + 2; r += kConvThreads / 32) {
-    const float* rowp = img + (i0 + r) * stride + j0;  // first needed element of staged row r
-    const int sh = conv_shift(rowp);
-    if (lane == 0) shs[r] = sh;
     if (i0 + r >= rows + 2) continue;  // feeds no stored output: left unstaged
+    const float* rowp = img + (i0 + r) * stride + j0;  // first needed element of staged row r
+    const int sh = shs[r];
     const float* lo = rowp - sh;
+    const uint32_t nf = ((uint32_t)(sh + need) + 3u) & ~3u;
+    if (lo >= img && lo + nf <= img_end) continue;  // a bulk-copied row
     const float* hi = rowp + need < img_end ? rowp + need : img_end;
     for (int ch = lane; ch < kConvChunks; ch += 32) {
       const float* e0 = lo + 4 * ch;
@@ -184,7 +242,16 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
   for (int k = 0; k < 9; ++k) w9[k] = f2_splat(__ldg(w + k));
   const f2 z2 = f2_splat(neg_zero);  // -0.0, unknown to the compiler: see f2_mac_z
   cp_wait<0>();
+  // Bounded wait for the bulk copies: 1 s on %globaltimer, then the launch
+  // flags a timeout and the block skips its outputs (after a second bounded
+  // wait, so no copy is still writing this block's shared memory at exit).
+  bool landed = conv_bar_wait(&bar);
+  if (!landed) {
+    if (threadIdx.x == 0) atomicOr(flag, 0x100u);
+    conv_bar_wait(&bar);
+  }
   __syncthreads();
+  if (!landed) return;
 
   const int c = threadIdx.x;
   f2 acc[P];
@@ -219,6 +286,7 @@ __global__ void __launch_bounds__(kConvThreads) conv3x3_kernel(const float* __re
     }
   }
 }
+
 
 }  // namespace
 
@@ -255,7 +323,7 @@ int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, ui
 }
 
 int launch_conv3x3(cudaStream_t s, int sms, const float* w, const float* img, uint64_t img_len, uint64_t stride,
-                   float* out, uint64_t rows, uint64_t cols, float seed) {
+                   float* out, uint64_t rows, uint64_t cols, float seed, unsigned* flag) {
   const uint64_t bx = (cols + kConvCols - 1) / kConvCols;
   if (bx > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
   // 16-row strips when they give every SM a few blocks, 4-row strips
@@ -264,11 +332,11 @@ int launch_conv3x3(cudaStream_t s, int sms, const float* w, const float* img, ui
   const uint64_t by16 = (rows + 15) / 16, by4 = (rows + 3) / 4;
   if (bx * by16 >= 4ull * (uint64_t)sms && by16 <= 65535) {
     conv3x3_kernel<16><<<dim3((unsigned)bx, (unsigned)by16), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
-                                                                                   rows, cols, seed, -0.0f);
+                                                                                   rows, cols, seed, -0.0f, flag);
   } else {
     if (by4 > 65535) return MAPAL_ERR_UNSUPPORTED;
     conv3x3_kernel<4><<<dim3((unsigned)bx, (unsigned)by4), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
-                                                                                 rows, cols, seed, -0.0f);
+                                                                                 rows, cols, seed, -0.0f, flag);
   }
   count_launch();
   return 0;

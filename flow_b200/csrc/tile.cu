@@ -14,7 +14,7 @@
 int launch_fir(cudaStream_t s, const float* w, uint64_t taps, const float* x, uint64_t x_len, float* y,
                uint64_t n_out, float seed);
 int launch_conv3x3(cudaStream_t s, int sms, const float* w, const float* img, uint64_t img_len, uint64_t stride,
-                   float* out, uint64_t rows, uint64_t cols, float seed);
+                   float* out, uint64_t rows, uint64_t cols, float seed, unsigned* flag);
 
 namespace {
 
@@ -133,7 +133,7 @@ int run_site(MapalGpuCtx* ctx, int local, const MapalTileSite& s, const float* a
   }
   if (is_conv3x3(s)) {
     int rc = launch_conv3x3(d.stream, d.prof.sm_count, a + s.a.base, b + s.b.base, s.b.len - s.b.base, s.b.ci, out, s.rows,
-                            s.c, s.seed);
+                            s.c, s.seed, d.trap);
     if (rc != MAPAL_ERR_UNSUPPORTED) return rc;
   }
   return launch_generic(d, s, a, b, out);

@@ -20,7 +20,8 @@ import math
 
 import flow_b200 as fb
 
-SITES = ("saxpy", "transpose", "gather", "sum", "fir", "conv2d", "matmul", "map_expr", "floor_empty", "floor_read")
+SITES = ("saxpy", "transpose", "gather", "sum", "sum_strict", "fir", "conv2d", "matmul", "map_expr", "tile_generic",
+         "gen", "floor_empty", "floor_read", "floor_random")
 
 
 def _alloc(torch, n, dtype=None):
@@ -117,6 +118,51 @@ def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = f
         per = 4 * n
         run = lambda s: ctx.map_expr(prog, [], s[0], n)
         flops = 0
+    elif name == "sum_strict":
+        # the interpreter-order fold (one dependent chain of f32 adds)
+        def mk(i):
+            x, out = _alloc(torch, n), _alloc(torch, 1)
+            ctx.gen(x, 1, 0, fb.U01)
+            return (x, out)
+        per = 4 * n
+        run = lambda s: ctx.fold_sum_strict(s[0], s[1])
+        flops = n
+    elif name == "tile_generic":
+        # a TileSite no specialised kernel takes: C = A * B^T read in place
+        # (b{ck=1, clane=K}), side x side x k, the rung-0 shape kernel
+        from .records import TileSite
+        side = int(math.isqrt(n))
+        kk = k or 64
+        site = TileSite()
+        site.rows, site.c, site.k = side, side, kk
+        site.a.ci, site.a.ck, site.a.len = kk, 1, side * kk
+        site.b.ck, site.b.clane, site.b.len = 1, kk, side * kk
+        site.mul_a_first, site.add_acc_first = 1, 1
+
+        def mk(i):
+            A, B, C = _alloc(torch, side * kk), _alloc(torch, side * kk), _alloc(torch, side * side)
+            ctx.gen(A, 2, 0)
+            ctx.gen(B, 2, side * kk)
+            return (A, B, C)
+        per = 4 * (2 * side * kk + side * side)
+        run = lambda s: ctx.tile_site(site, s[0], s[1], s[2])
+        flops = 2 * side * side * kk
+    elif name == "gen":
+        # the seeded uniform stream written to n floats
+        def mk(i):
+            return (_alloc(torch, n),)
+        per = 4 * n
+        run = lambda s: ctx.gen(s[0], 1, 0)
+        flops = 0
+    elif name == "floor_random":
+        # n independent random 4-byte reads of x (the gather's bound)
+        def mk(i):
+            x, sink = _alloc(torch, n), _alloc(torch, 1)
+            ctx.gen(x, 1, 0)
+            return (x, sink)
+        per = 4 * n
+        run = lambda s: ctx.probe_launch_floor(2, s[0], s[1])
+        flops = 0
     elif name == "floor_empty":
         # the launch floor: an empty kernel
         def mk(i):
@@ -205,7 +251,8 @@ def main() -> int:
     import torch
     defaults = {"saxpy": 1 << 20, "transpose": 1024 * 1024, "gather": 1 << 20, "sum": 1 << 20,
                 "fir": 1 << 20, "conv2d": 1024 * 1024, "matmul": 4096, "map_expr": 1 << 20, "floor_empty": 1,
-                "floor_read": 1 << 20}
+                "floor_read": 1 << 20, "sum_strict": 1 << 20, "tile_generic": 1024 * 1024, "gen": 1 << 26,
+                "floor_random": 1 << 26}
     sites = SITES if args.site == "all" else (args.site,)
     with fb.Context((0,), sync=False) as ctx:
         l2 = ctx.profile().l2_bytes

@@ -148,7 +148,13 @@ typedef struct MapalGpuProfile {
                                  interpreter's order: bit-identical */
 #define MAPAL_MATMUL_TF32X3 1 /* tcgen05 tensor cores, 3xTF32 split; opt-in,
                                  within a stated relative error (ADR-0032's
-                                 tf32-class contract) */
+                                 tf32-class contract): per cell
+                                 |C - A.B| <= 2e-6 * ||A_i,:|| * ||B_:,j|| for
+                                 K <= 4096 (the tensor pipe's accumulation
+                                 error grows with K; B200-measured at most
+                                 1.1e-6 at K = 4096 and 1.9e-6 at K = 16384).
+                                 A cell that reads a NaN is NaN; one that
+                                 reads an infinity is not finite. */
 
 /* generator kinds for mapal_gpu_gen_f32 */
 #define MAPAL_GEN_U11 0 /* uniform[-1,1) */
@@ -372,7 +378,7 @@ int mapal_gpu_conv2d_3x3_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const 
 /* matmul site (benches/matmul/matmul1024_cap_f32.mapal:7-11): rows=M, c=N, k=K,
  * a = A {ci=lda, ck=1, clane=0}, b = B {ci=0, ck=ldb, clane=1}, out row-major M x N.
  * mode MAPAL_MATMUL_STRICT is bit-identical with the interpreter;
- * MAPAL_MATMUL_TF32X3 is within max|C - C_ref| <= 1e-5 * ||A_i,:|| * ||B_:,j||. */
+ * MAPAL_MATMUL_TF32X3 is within the bound stated at its definition. */
 int mapal_gpu_matmul_f32(MapalGpuCtx* ctx, const MapalTileSite* site, const float* A,
                          const float* B, float* C, int mode);
 
@@ -448,8 +454,10 @@ int mapal_gpu_gather_sharded(MapalGpuCtx* ctx, const float* const* x, uint64_t n
 /* Row-block matmul: device d holds its row block A[d] (m[d] rows x K) and a
  * full B buffer B[d]; B on global rank `root` is broadcast to all B[d] first
  * (NCCL), then each device computes C[d] = A[d] * B. site describes the full
- * problem (rows = total M). Strict mode stays bit-exact: each cell's k order
- * is untouched by the row split. */
+ * problem (rows = total M). Over several ranks with K >= 512 the broadcast runs
+ * in k-ranges overlapped with the multiply of the previous range. Strict mode
+ * stays bit-exact: each cell's k order is untouched by the row split and the
+ * ranges; in 3xTF32 mode each later range adds its product to C. */
 int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSite* site,
                                  const float* const* A, float* const* B, float* const* C,
                                  const uint64_t* m, int root, int mode);
@@ -469,7 +477,9 @@ int mapal_gpu_probe_mma_peak(MapalGpuCtx* ctx, int kind, uint32_t iters, double*
 /* No counterpart in the reference: the floor under the 2^20-element sites.
  * kind 0 launches an empty kernel; kind 1 reads x (n floats, n a multiple of
  * 4, 16-byte aligned) with the sum fold's own grid and loads but no combine
- * across blocks (`sink`, a device float, is written only to keep the loads).
+ * across blocks; kind 2 makes n independent 4-byte reads of x at hashed
+ * positions in [0, n) (the gather's bound: random reads, no index array, no
+ * output). `sink`, a device float, is written only to keep the loads.
  * Enqueued on local device 0's stream; time it as the sites are timed. */
 int mapal_gpu_probe_launch_floor(MapalGpuCtx* ctx, int kind, const float* x, uint64_t n, float* sink);
 

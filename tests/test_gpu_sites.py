@@ -320,6 +320,22 @@ def test_conv2d_random_valid(ctx, H, W):
     assert same_bits(host(out), want), first_diff(host(out), want)
 
 
+@pytest.mark.parametrize("H,W,base", [(4098, 4098, 0), (2051, 3001, 0), (2051, 3001, 3), (1800, 6000, 1)])
+def test_conv2d_large_sites(ctx, H, W, base):
+    # sites of four or more 16-row strips per SM take the persistent,
+    # double-buffered kernel: square, ragged, and an image that starts off
+    # the 16-byte boundary (its first rows are staged by the edge path)
+    img = o.gen(base + H * W, 2, 0)
+    w = o.gen(9, 2, base + H * W)
+    R, C = H - 2, W - 2
+    site = fb.conv2d_site(R, C, W, base + H * W)
+    site.b.base = base
+    out = empty_f32(R * C)
+    ctx.conv2d_3x3(site, dev(w), dev(img), out)
+    want = o.conv2d_3x3(w, img[base:].copy(), W, R, C)
+    assert same_bits(host(out), want), first_diff(host(out), want)
+
+
 # ---- matmul strict ----------------------------------------------------------------------------------
 
 @pytest.mark.parametrize("case", GOLD["matmul_known_answers"], ids=lambda c: f"n{c['n']}")

@@ -101,21 +101,37 @@ __global__ void __launch_bounds__(kThreads) fold_sum_kernel(const float* __restr
   if (kVec) {
     const float4* x4 = reinterpret_cast<const float4*>(x);
     const uint64_t n4 = n / 4;
-    // Four 16-byte loads per thread per trip, predicated and issued together,
-    // so a small input costs one memory round trip.
-    for (uint64_t i = gid; i < n4; i += 4 * stride) {
+    // Four 16-byte loads per thread per trip, issued together; the last,
+    // partial trip loads a clamped (valid) index and zeroes what lies past
+    // the end with a select, so its loads are not behind branches either and
+    // a small input costs one memory round trip.
+    uint64_t i = gid;
+    for (; i + 3 * stride < n4; i += 4 * stride) {
       float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const uint64_t j = i + u * stride;
-        v[u] = j < n4 ? __ldcs(x4 + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
+      for (int u = 0; u < 4; ++u) v[u] = __ldcs(x4 + i + u * stride);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         acc += (double)v[u].x;
         acc += (double)v[u].y;
         acc += (double)v[u].z;
         acc += (double)v[u].w;
+      }
+    }
+    if (i < n4) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint64_t j = i + u * stride;
+        v[u] = __ldcs(x4 + (j < n4 ? j : n4 - 1));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const bool in = i + u * stride < n4;
+        acc += in ? (double)v[u].x : 0.0;
+        acc += in ? (double)v[u].y : 0.0;
+        acc += in ? (double)v[u].z : 0.0;
+        acc += in ? (double)v[u].w : 0.0;
       }
     }
     tail = n4 * 4;
@@ -332,15 +348,24 @@ __global__ void __launch_bounds__(kThreads) floor_read_kernel(const float4* __re
   const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
   const uint64_t gid = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x;
   float acc = 0.0f;
-  for (uint64_t i = gid; i < n4; i += 4 * stride) {
+  uint64_t i = gid;
+  for (; i + 3 * stride < n4; i += 4 * stride) {
+    float4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldcs(x4 + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) acc += v[u].x + v[u].y + v[u].z + v[u].w;
+  }
+  if (i < n4) {
     float4 v[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const uint64_t j = i + u * stride;
-      v[u] = j < n4 ? __ldcs(x4 + j) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      v[u] = __ldcs(x4 + (j < n4 ? j : n4 - 1));
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) acc += v[u].x + v[u].y + v[u].z + v[u].w;
+    for (int u = 0; u < 4; ++u)
+      if (i + u * stride < n4) acc += v[u].x + v[u].y + v[u].z + v[u].w;
   }
   if (acc == 1.2345e-30f) *sink = acc;  // practically never: keeps the loads
 }

@@ -326,16 +326,20 @@ int launch_conv3x3(cudaStream_t s, int sms, const float* w, const float* img, ui
                    float* out, uint64_t rows, uint64_t cols, float seed, unsigned* flag) {
   const uint64_t bx = (cols + kConvCols - 1) / kConvCols;
   if (bx > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
-  // 16-row strips when they give every SM a few blocks, 4-row strips
-  // otherwise (B200, 4098^2 and 8194^2 images: 16 rows beat 4, 8 and 32 by
-  // 4-25 %; at 1026^2 4 rows win: the grid is the limit there).
-  const uint64_t by16 = (rows + 15) / 16, by4 = (rows + 3) / 4;
-  if (bx * by16 >= 4ull * (uint64_t)sms && by16 <= 65535) {
-    conv3x3_kernel<16><<<dim3((unsigned)bx, (unsigned)by16), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
+  // 10-row strips when they give every SM a few blocks, 2-row strips
+  // otherwise. B200, bulk-copy staging, 4098^2 / 8194^2 images: 8, 9, 10, 11,
+  // 12, 14, 16, 24 and 32 rows measured 28.7, 25.9, 25.7, 26.0, 27.1, 29.2,
+  // 30.4, 31.5 and 34.9 us / 95.4, 86.1, 85.9, 85.6, 88.9, 90.9, 95.5, 100.1
+  // and 118.2 us (0.80 / 0.95 of the copy rate at 10 rows); at 1026^2 the grid
+  // is the limit: 2, 3, 4, 6 and 8 rows took 3.86, 4.06, 4.2-4.4, 4.20 and
+  // 4.46 us (more, shorter blocks in flight).
+  const uint64_t by10 = (rows + 9) / 10, by2 = (rows + 1) / 2;
+  if (bx * by10 >= 4ull * (uint64_t)sms && by10 <= 65535) {
+    conv3x3_kernel<10><<<dim3((unsigned)bx, (unsigned)by10), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
                                                                                    rows, cols, seed, -0.0f, flag);
   } else {
-    if (by4 > 65535) return MAPAL_ERR_UNSUPPORTED;
-    conv3x3_kernel<4><<<dim3((unsigned)bx, (unsigned)by4), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
+    if (by2 > 65535) return MAPAL_ERR_UNSUPPORTED;
+    conv3x3_kernel<2><<<dim3((unsigned)bx, (unsigned)by2), kConvThreads, 0, s>>>(w, img, img_len, stride, out,
                                                                                  rows, cols, seed, -0.0f, flag);
   }
   count_launch();

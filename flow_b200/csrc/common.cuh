@@ -184,8 +184,5 @@ int validate_tile_site(const MapalTileSite* site, const void* a, const void* b, 
 int slot_events(DeviceSlot& d, size_t n);
 int nccl_broadcast_f32_on(MapalGpuCtx* ctx, float* const* buf, size_t offset, size_t count, int root,
                           bool on_comm);
-// acc_from_c: add the product to C as it stands instead of to the seed (a
-// later k-range of a product split along K).
 int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C, uint64_t M,
-                         uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed,
-                         int acc_from_c = 0);
+                         uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed);

@@ -179,8 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mm_tf32x3_kernel(const __grid_constant__ CUtensorMap map_ahi, const __grid_constant__ CUtensorMap map_alo,
                      const __grid_constant__ CUtensorMap map_bhi, const __grid_constant__ CUtensorMap map_blo,
                      float* __restrict__ C, int M, int N, int K, long long ldc, float seed, unsigned* flag,
-                     int tiles_m, int tiles_n, int tile_base, int nsplit, float* __restrict__ part_out,
-                     int acc_c) {
+                     int tiles_m, int tiles_n, int tile_base, int nsplit, float* __restrict__ part_out) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -292,16 +291,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nvalid = N - (n0 + c0);
           if (nvalid >= 32 && ((ldc & 3) == 0) && (((uintptr_t)C & 15) == 0)) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              // acc_c: a later k-range adds its product to the partial C
-              const float4 base = acc_c ? *reinterpret_cast<const float4*>(crow + j) : make_float4(seed, seed, seed, seed);
+            for (int j = 0; j < 32; j += 4)
               *reinterpret_cast<float4*>(crow + j) =
-                  make_float4(base.x + v[j], base.y + v[j + 1], base.z + v[j + 2], base.w + v[j + 3]);
-            }
+                  make_float4(v[j] + seed, v[j + 1] + seed, v[j + 2] + seed, v[j + 3] + seed);
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (j < nvalid) crow[j] = (acc_c ? crow[j] : seed) + v[j];
+              if (j < nvalid) crow[j] = v[j] + seed;
           }
         }
       }
@@ -327,7 +323,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // so the result is the same on every run.
 __global__ void reduce_parts_kernel(const float* __restrict__ part, float* __restrict__ C, int M, int N,
                                     long long ldc, float seed, int tiles_m, int tiles_n, int tile_base, int ntiles,
-                                    int nsplit, int acc_c) {
+                                    int nsplit) {
   const long long total = (long long)ntiles * BM * BN;
   for (long long e = blockIdx.x * (long long)blockDim.x + threadIdx.x; e < total;
        e += (long long)gridDim.x * blockDim.x) {
@@ -339,8 +335,7 @@ __global__ void reduce_parts_kernel(const float* __restrict__ part, float* __res
     if (m >= M || n >= N) continue;
     float acc = 0.0f;
     for (int p = 0; p < nsplit; ++p) acc += part[((long long)r * nsplit + p) * (BM * BN) + within];
-    float* c = C + (long long)m * ldc + n;
-    *c = (acc_c ? *c : seed) + acc;
+    C[(long long)m * ldc + n] = acc + seed;
   }
 }
 
@@ -393,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mm_tf32x3_fused_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_bhi,
                            const __grid_constant__ CUtensorMap map_blo, float* __restrict__ C, int M, int N, int K,
                            long long ldc, float seed, unsigned* flag, int tiles_m, int tiles_n, int tile_base,
-                           int nsplit, float* __restrict__ part_out, int acc_c) {
+                           int nsplit, float* __restrict__ part_out) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SmemF& sm = *reinterpret_cast<SmemF*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -520,16 +515,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int nvalid = N - (n0 + c0);
           if (nvalid >= 32 && ((ldc & 3) == 0) && (((uintptr_t)C & 15) == 0)) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              // acc_c: a later k-range adds its product to the partial C
-              const float4 base = acc_c ? *reinterpret_cast<const float4*>(crow + j) : make_float4(seed, seed, seed, seed);
+            for (int j = 0; j < 32; j += 4)
               *reinterpret_cast<float4*>(crow + j) =
-                  make_float4(base.x + v[j], base.y + v[j + 1], base.z + v[j + 2], base.w + v[j + 3]);
-            }
+                  make_float4(v[j] + seed, v[j + 1] + seed, v[j + 2] + seed, v[j + 3] + seed);
           } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-              if (j < nvalid) crow[j] = (acc_c ? crow[j] : seed) + v[j];
+              if (j < nvalid) crow[j] = v[j] + seed;
           }
         }
       }
@@ -797,7 +789,7 @@ int make_map(CUtensorMap* map, const float* base, uint64_t rows, uint64_t K, uin
 }  // namespace
 
 int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C, uint64_t M, uint64_t N,
-                         uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed, int acc_from_c) {
+                         uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed) {
   if (M > 0x7fffffffull || N > 0x7fffffffull || K > 0x7fffffffull) return set_error(MAPAL_ERR_UNSUPPORTED, "too large");
   if ((N + BN - 1) / BN > 0x7fffffffull || (M + BM - 1) / BM > 65535)
     return set_error(MAPAL_ERR_UNSUPPORTED, "matmul grid too large");
@@ -855,19 +847,18 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
     }
     if (whole > 0) {
       mm_tf32x3_fused_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(
-          m_a, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, 0, 1, nullptr,
-          acc_from_c);
+          m_a, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, 0, 1, nullptr);
       count_launch();
     }
     if (nsplit > 1) {
       mm_tf32x3_fused_kernel<<<(unsigned)(rem * nsplit), kThreads, smem, d.stream>>>(
           m_a, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, full, nsplit,
-          parts, 0);
+          parts);
       count_launch();
       const uint64_t n_red = (uint64_t)rem * BM * BN;
       reduce_parts_kernel<<<stream_grid(n_red, 256, sms, 8), 256, 0, d.stream>>>(parts, C, (int)M, (int)N,
                                                                                 (long long)ldc, seed, tiles_m, tiles_n,
-                                                                                full, rem, nsplit, acc_from_c);
+                                                                                full, rem, nsplit);
       count_launch();
     }
     return 0;
@@ -892,18 +883,18 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   if (whole > 0) {
     mm_tf32x3_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N,
                                                                     (int)K, (long long)ldc, seed, d.trap, tiles_m,
-                                                                    tiles_n, 0, 1, nullptr, acc_from_c);
+                                                                    tiles_n, 0, 1, nullptr);
     count_launch();
   }
   if (nsplit > 1) {
     mm_tf32x3_kernel<<<(unsigned)(rem * nsplit), kThreads, smem, d.stream>>>(
         m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, full,
-        nsplit, parts, 0);
+        nsplit, parts);
     count_launch();
     const uint64_t n_red = (uint64_t)rem * BM * BN;
     reduce_parts_kernel<<<stream_grid(n_red, 256, sms, 8), 256, 0, d.stream>>>(parts, C, (int)M, (int)N,
                                                                               (long long)ldc, seed, tiles_m, tiles_n,
-                                                                              full, rem, nsplit, acc_from_c);
+                                                                              full, rem, nsplit);
     count_launch();
   }
   return 0;

@@ -37,19 +37,18 @@ int check_arrays(MapalGpuCtx* ctx, const void* a, const void* b, const void* c) 
   return 0;
 }
 
-// Row-block matmul with the B broadcast overlapped: K is cut into up to
-// kChunks ranges, [0, K/8), [K/8, 3K/8), [3K/8, K) (cuts rounded up to whole
-// 64-deep k-tiles); the broadcast of B's rows for range c runs on the comm
-// stream while range c-1 is multiplied on the compute stream, so only the
-// first eighth of B's transfer is exposed and each range's multiply is
-// longer than the next range's transfer. Strict: range c > 0 continues every
-// cell from the partial fold range c-1 left in C, so each cell still folds
-// k = 0..K-1 in order from the seed, bit-identical to one pass. 3xTF32: range
-// c > 0 adds its product to C (one more f32 rounding per range).
+// Strict row-block matmul with the B broadcast overlapped: K is cut into up
+// to kChunks ranges, [0, K/8), [K/8, 3K/8), [3K/8, K) (cuts rounded up to
+// whole 64-deep k-tiles); the broadcast of B's rows for range c runs on the
+// comm stream while range c-1 is multiplied on the compute stream, so only
+// the first eighth of B's transfer is exposed and each range's multiply is
+// longer than the next range's transfer. Range c > 0 continues every cell
+// from the partial fold range c-1 left in C, so each cell still folds
+// k = 0..K-1 in order from the seed: bit-identical to one pass.
 constexpr int kChunks = 3;
 
 int matmul_sharded_overlapped(MapalGpuCtx* ctx, const MapalTileSite* site, const float* const* A,
-                              float* const* B, float* const* C, const uint64_t* m, int root, int mode) {
+                              float* const* B, float* const* C, const uint64_t* m, int root) {
   const uint64_t K = site->k, lda = site->a.ci, ldb = site->b.ck, N = site->c;
   const int nd = (int)ctx->dev.size();
   // Validate every device's record before anything is enqueued.
@@ -100,15 +99,11 @@ int matmul_sharded_overlapped(MapalGpuCtx* ctx, const MapalTileSite* site, const
       MAPAL_CUDA(cudaStreamWaitEvent(d.stream, d.events[c], 0));
       if (m[i] == 0) continue;
       const uint64_t k0 = k_lo[c], kc = k_lo[c + 1] - k_lo[c];
-      if (mode == MAPAL_MATMUL_TF32X3)
-        MAPAL_TRY(launch_matmul_tf32x3(d, A[i] + k0, B[i] + site->b.base + k0 * ldb, C[i], m[i], N, kc, lda, ldb, N,
-                                       site->seed, c > 0 ? 1 : 0));
-      else
-        MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, A[i] + k0, B[i] + site->b.base + k0 * ldb,
-                                          C[i], m[i], N, kc, lda, ldb, N, site->seed, c > 0 ? 1 : 0));
+      MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, A[i] + k0, B[i] + site->b.base + k0 * ldb,
+                                        C[i], m[i], N, kc, lda, ldb, N, site->seed, c > 0 ? 1 : 0));
     }
   }
-  return finish_all(ctx, mode == MAPAL_MATMUL_TF32X3);
+  return finish_all(ctx, false);
 }
 
 }  // namespace
@@ -201,7 +196,8 @@ extern "C" int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSit
     return set_error(MAPAL_ERR_INVALID, "unknown matmul mode");
   if (root < 0 || root >= ctx->nranks) return set_error(MAPAL_ERR_INVALID, "root out of range");
   const uint64_t b_elems = site->b.len;
-  if (ctx->nranks > 1 && site->k >= 512) return matmul_sharded_overlapped(ctx, site, A, B, C, m, root, mode);
+  if (mode == MAPAL_MATMUL_STRICT && ctx->nranks > 1 && site->k >= 512)
+    return matmul_sharded_overlapped(ctx, site, A, B, C, m, root);
   // B is replicated first: every rank's full B buffer receives root's.
   MAPAL_TRY(nccl_broadcast_f32(ctx, B, b_elems, root));
   for (int i = 0; i < (int)ctx->dev.size(); ++i) {

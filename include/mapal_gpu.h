@@ -454,10 +454,10 @@ int mapal_gpu_gather_sharded(MapalGpuCtx* ctx, const float* const* x, uint64_t n
 /* Row-block matmul: device d holds its row block A[d] (m[d] rows x K) and a
  * full B buffer B[d]; B on global rank `root` is broadcast to all B[d] first
  * (NCCL), then each device computes C[d] = A[d] * B. site describes the full
- * problem (rows = total M). Over several ranks with K >= 512 the broadcast runs
- * in k-ranges overlapped with the multiply of the previous range. Strict mode
- * stays bit-exact: each cell's k order is untouched by the row split and the
- * ranges; in 3xTF32 mode each later range adds its product to C. */
+ * problem (rows = total M). In strict mode over several ranks with K >= 512
+ * the broadcast runs in k-ranges overlapped with the multiply of the previous
+ * range; strict mode stays bit-exact, as each cell's k order is untouched by
+ * the row split and the ranges. */
 int mapal_gpu_matmul_f32_sharded(MapalGpuCtx* ctx, const MapalTileSite* site,
                                  const float* const* A, float* const* B, float* const* C,
                                  const uint64_t* m, int root, int mode);

@@ -128,8 +128,7 @@ def test_matmul_sharded(ctx, mode):
     else:
         A2, B2 = A.reshape(M, K).astype(np.float64), B.reshape(K, N).astype(np.float64)
         scale = np.sqrt((A2 ** 2).sum(1))[:, None] * np.sqrt((B2 ** 2).sum(0))[None, :]
-        # the stated 3xTF32 bound (over several ranks K is multiplied in
-        # ranges, each adding its product to C)
+        # the stated 3xTF32 bound
         exact = A2 @ B2
         assert np.max(np.abs(got.reshape(M, N) - exact) / scale) <= 2e-6
 

@@ -276,7 +276,7 @@ def test_fir_golden(ctx, n):
 
 
 @pytest.mark.parametrize("n,taps", [(1, 1), (100, 7), (1000, 8), (4097, 16), ((1 << 20) - 63, 64), (3000, 100),
-                                    (10000, 1000)])
+                                    (10000, 1000), (3, 16), (2049, 32), (2047, 64), (6145, 64), (100003, 32)])
 def test_fir_random(ctx, n, taps):
     x = o.gen(n + taps - 1, 1, 0)
     w = o.gen(taps, 1, n + taps - 1)

@@ -28,7 +28,9 @@ pytestmark = pytest.mark.gpu
 GOLD = json.load(open(os.path.join(os.path.dirname(__file__), "golden", "reference_outputs.json")))
 TOL = 2e-6
 SHAPES = [(128, 256, 16), (256, 256, 256), (200, 300, 100), (129, 257, 33), (64, 64, 30), (1, 1, 1),
-          (1024, 1024, 1024), (300, 700, 4096)]
+          (1024, 1024, 1024), (300, 700, 4096),
+          # K a multiple of 4 (A read in place by the fused kernel) below one 16-deep k-block
+          (130, 270, 4), (64, 64, 8), (257, 129, 12), (100, 33, 20)]
 
 
 @pytest.fixture(scope="module")

@@ -10,7 +10,7 @@ import oracle as o
 
 TOL = 2e-6  # the bound of tests/test_gpu_tf32x3.py and include/mapal_gpu.h
 SHAPES = [(128, 256, 16), (256, 256, 256), (200, 300, 100), (129, 257, 33), (64, 64, 30), (1, 1, 1),
-          (1024, 1024, 1024), (300, 700, 4096)]
+          (1024, 1024, 1024), (300, 700, 4096), (130, 270, 4), (64, 64, 8), (257, 129, 12), (100, 33, 20)]
 
 
 def rna_tf32(x: np.ndarray) -> np.ndarray:
@@ -49,5 +49,5 @@ def test_tf32x3_tolerance_rejects_fewer_products(M, N, K):
     two_b = norm_err(ahi @ bhi + alo @ bhi, ref, A2, B2)
     one = norm_err(ahi @ bhi, ref, A2, B2)
     # the split itself is far inside the bound; every reduced form is outside it
-    assert three < TOL / 20
+    assert three < TOL / 10
     assert min(two_a, two_b, one) > 5 * TOL, (two_a, two_b, one)

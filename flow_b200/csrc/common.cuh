@@ -174,9 +174,12 @@ int launch_fold_sum_peer(cudaStream_t s, int sms, const float* x, uint64_t n, fl
 int peer_setup(MapalGpuCtx* ctx);
 int launch_matmul_strict(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
                          uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed);
+// acc_from_c: continue every cell from C's value (a later k-range).
+// beside_collective: an SM-based collective (an NCCL kernel) runs beside
+// this launch, so the plan keeps a part-filled wave for it to run in.
 int launch_matmul_strict_ex(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
                             uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed,
-                            int acc_from_c);
+                            int acc_from_c, int beside_collective);
 // Record checks of tile.cu: status, and whether the record is matmul-shaped.
 int validate_tile_site(const MapalTileSite* site, const void* a, const void* b, const void* out, bool* empty,
                        bool* matmul_shaped);

@@ -153,7 +153,7 @@ int host_one(MapalGpuCtx* ctx, int i, const MapalTileSite* site, const float* A,
       MAPAL_CUDA(cudaStreamWaitEvent(d.stream, ev[2 + c], 0));
       if (c + 1 < nph) {
         MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, dA + k0, dB + b_lo, dC, M, N, kc, lda, ldb, N,
-                                          site->seed, c > 0));
+                                          site->seed, c > 0, 0));
         continue;
       }
       // the row blocks alternate between two streams, so one block's last
@@ -166,7 +166,7 @@ int host_one(MapalGpuCtx* ctx, int i, const MapalTileSite* site, const float* A,
         cudaEvent_t done = ev[2 + nph + blk];
         cudaStream_t cs = blk % 2 ? d.aux_stream : d.stream;
         MAPAL_TRY(launch_matmul_strict_ex(cs, d.prof.sm_count, dA + r0 * lda + k0, dB + b_lo, dC + r0 * N,
-                                          r1 - r0, N, kc, lda, ldb, N, site->seed, c > 0));
+                                          r1 - r0, N, kc, lda, ldb, N, site->seed, c > 0, 0));
         MAPAL_CUDA(cudaEventRecord(done, cs));
         MAPAL_CUDA(cudaStreamWaitEvent(d.d2h_stream, done, 0));
         MAPAL_CUDA(cudaMemcpyAsync(C + r0 * N, dC + r0 * N, (r1 - r0) * N * 4, cudaMemcpyDeviceToHost,
@@ -331,8 +331,9 @@ extern "C" int mapal_gpu_matmul_f32_host_sharded(MapalGpuCtx* ctx, const MapalTi
       if (!M) continue;
       const float* bk = dB[i] + k0 * ldb;
       if (c + 1 < nph) {
+        // the next phase's B rows are gathered by NCCL beside this multiply
         MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, dA[i] + k0, bk, dC[i], M, N, kc, lda, ldb, N,
-                                          site->seed, c > 0));
+                                          site->seed, c > 0, 1));
         continue;
       }
       MAPAL_CUDA(cudaEventRecord(ev[2 + 2 * nph + nblocks[i]], d.stream));
@@ -343,7 +344,7 @@ extern "C" int mapal_gpu_matmul_f32_host_sharded(MapalGpuCtx* ctx, const MapalTi
         cudaEvent_t done = ev[2 + 2 * nph + blk];
         cudaStream_t cs = blk % 2 ? d.aux_stream : d.stream;
         MAPAL_TRY(launch_matmul_strict_ex(cs, d.prof.sm_count, dA[i] + r0 * lda + k0, bk, dC[i] + r0 * N,
-                                          r1 - r0, N, kc, lda, ldb, N, site->seed, c > 0));
+                                          r1 - r0, N, kc, lda, ldb, N, site->seed, c > 0, 0));
         MAPAL_CUDA(cudaEventRecord(done, cs));
         MAPAL_CUDA(cudaStreamWaitEvent(d.d2h_stream, done, 0));
         MAPAL_CUDA(cudaMemcpyAsync(C[i] + r0 * N, dC[i] + r0 * N, (r1 - r0) * N * 4, cudaMemcpyDeviceToHost,

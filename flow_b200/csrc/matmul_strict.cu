@@ -20,7 +20,11 @@
 //    argument that this is bit-identical to a rounded multiply then a
 //    rounded add), leaving issue slots for the loads so the FP32 pipe, not
 //    issue, is the bound;
-//  * no split-K: k is never partitioned, so no cell is reassociated.
+//  * no split-K: k is never partitioned, so no cell is reassociated;
+//  * the launch plan covers the site with whole waves of 128 x 128 tiles and
+//    a remainder of 64 x 64 tiles, or with 128 x 112 tiles where 148 = 4 x 37
+//    SMs leave the 128-wide plan a part-filled wave (row blocks of 512 or
+//    1024 rows and 4096 columns, as a row-sharded 4096^2 site gives each GPU).
 //
 // The roofline is the FP32 pipe at one operation per lane per clock
 // (148 SMs x 128 lanes), i.e. half the FFMA-counted peak: a strict MAC is two
@@ -240,6 +244,179 @@ __global__ void __launch_bounds__(Cfg<BM, BN, BK, TM, TN, STAGES>::kThreads, 1)
   }
 }
 
+// 128 x 112 tiles. 148 SMs = 4 x 37 and 37 x 112 = 4144, so a block of
+// 128·r rows and up to 4144 columns is r/4 waves with no partly empty wave
+// (512 x 4096 is exactly one), where 128 x 128 tiles leave 20 of 148 SMs idle
+// or run a part-filled extra wave. The threads stay 256 (8 warps, two per
+// scheduler, as in the 128 x 128 kernel: 224 threads leave one scheduler with
+// a single warp and run no faster than 128 x 128), laid out 32 x 8, each
+// owning 4 rows x 14 columns: rows ty + 32i and columns 4tx .. 4tx+3,
+// 32 + 4tx .., 64 + 4tx .. and 96 + 2tx, 96 + 2tx+1 of the tile. So a warp's
+// B reads are three 128-byte and one 64-byte run per k, its A reads four
+// consecutive rows, and the 14 columns pair into 7 packed cells per row.
+// Every cell keeps its own chain: seed (or C), then one rounded product and
+// one rounded add per k, k ascending.
+constexpr int kNBM = 128, kNBN = 112, kNBK = 64, kNStages = 2, kNThreads = 256;
+constexpr int kNAStride = kNBK + 4, kNBStride = kNBN + 4;
+constexpr int kNAStage = kNBM * kNAStride, kNBStage = kNBK * kNBStride;
+constexpr size_t kNSmem = sizeof(float) * (size_t)kNStages * (kNAStage + kNBStage);
+static_assert((kNBM * kNBK / 4) % kNThreads == 0 && (kNBK * kNBN / 4) % kNThreads == 0, "whole loader trips");
+
+template <bool kVec>
+__global__ void __launch_bounds__(kNThreads, 1)
+    mm_strict_n112_kernel(const float* __restrict__ A, const float* __restrict__ B, float* __restrict__ C, int M,
+                          int N, int K, long long lda, long long ldb, long long ldc, float seed, int tile_base,
+                          int tiles_m, int tiles_n0, int acc_from_c, float neg_zero) {
+  const f2 z2 = f2_splat(neg_zero);  // -0.0, unknown to the compiler: see f2_mac_z
+  extern __shared__ __align__(16) float smem[];
+  float* As = smem;                          // [kNStages][128][kNAStride]
+  float* Bs = smem + kNStages * kNAStage;    // [kNStages][64][kNBStride]
+
+  const int tid = threadIdx.x;
+  const int tx = tid % 8, ty = tid / 8;
+  const int parent = tile_base + (int)blockIdx.x;
+  const int per_group = kGroupRows * tiles_n0;
+  const int grp = parent / per_group, in_grp = parent % per_group;
+  const int grp_rows = tiles_m - grp * kGroupRows < kGroupRows ? tiles_m - grp * kGroupRows : kGroupRows;
+  const int pm = grp * kGroupRows + in_grp % grp_rows, pn = in_grp / grp_rows;
+  const int m0 = pm * kNBM, n0 = pn * kNBN;
+  const int KT = (K + kNBK - 1) / kNBK;
+
+  auto load_tile = [&](int kt, int stage) {
+    const int k0 = kt * kNBK;
+    float* as = As + stage * kNAStage;
+    float* bs = Bs + stage * kNBStage;
+#pragma unroll
+    for (int g = tid; g < kNBM * kNBK / 4; g += kNThreads) {
+      const int row = g / (kNBK / 4), kq = g % (kNBK / 4);
+      const int m = m0 + row, k = k0 + kq * 4;
+      const int nvalid = (m < M) ? min(4, K - k) : 0;
+      copy4<kVec>(smem_u32(as + row * kNAStride + kq * 4),
+                  A + (long long)(m < M ? m : 0) * lda + (nvalid > 0 ? k : 0), nvalid);
+    }
+#pragma unroll
+    for (int g = tid; g < kNBK * kNBN / 4; g += kNThreads) {
+      const int kr = g / (kNBN / 4), nq = g % (kNBN / 4);
+      const int k = k0 + kr, n = n0 + nq * 4;
+      const int nvalid = (k < K) ? min(4, N - n) : 0;
+      copy4<kVec>(smem_u32(bs + kr * kNBStride + nq * 4),
+                  B + (long long)(k < K ? k : 0) * ldb + (nvalid > 0 ? n : 0), nvalid);
+    }
+  };
+
+  // acc[i][q]: row ty + 32i; q = 0..5 the column pairs of the three 4-column
+  // runs (4tx + 32·(q/2) + 2·(q%2)), q = 6 the pair at 96 + 2tx.
+  f2 acc[4][7];
+  const f2 s2 = f2_splat(seed);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int q = 0; q < 7; ++q) acc[i][q] = s2;
+  auto col = [&](int q) { return q < 6 ? 32 * (q >> 1) + 4 * tx + 2 * (q & 1) : 96 + 2 * tx; };
+
+  if (acc_from_c) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int m = m0 + ty + 32 * i;
+      const float* cp = C + (long long)(m < M ? m : 0) * ldc;
+#pragma unroll
+      for (int q = 0; q < 7; ++q) {
+        const int n = n0 + col(q);
+        const float lo = (m < M && n < N) ? cp[n] : 0.0f;
+        const float hi = (m < M && n + 1 < N) ? cp[n + 1] : 0.0f;
+        acc[i][q] = f2_pack(lo, hi);
+      }
+    }
+  }
+
+#pragma unroll
+  for (int s = 0; s < kNStages - 1; ++s) {
+    if (s < KT) load_tile(s, s);
+    cp_commit();
+  }
+
+  auto step = [&](const float (&av)[4], const float* brow) {
+    const float4 b0 = *reinterpret_cast<const float4*>(brow + 4 * tx);
+    const float4 b1 = *reinterpret_cast<const float4*>(brow + 32 + 4 * tx);
+    const float4 b2 = *reinterpret_cast<const float4*>(brow + 64 + 4 * tx);
+    const float2 b3 = *reinterpret_cast<const float2*>(brow + 96 + 2 * tx);
+    const f2 bp[7] = {f2_pack(b0.x, b0.y), f2_pack(b0.z, b0.w), f2_pack(b1.x, b1.y), f2_pack(b1.z, b1.w),
+                      f2_pack(b2.x, b2.y), f2_pack(b2.z, b2.w), f2_pack(b3.x, b3.y)};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const f2 a2 = f2_splat(av[i]);
+#pragma unroll
+      for (int q = 0; q < 7; ++q) acc[i][q] = f2_mac_z(acc[i][q], a2, bp[q], z2);
+    }
+  };
+
+  for (int kt = 0; kt < KT; ++kt) {
+    cp_wait<kNStages - 2>();
+    __syncthreads();
+    {
+      const int nt = kt + kNStages - 1;
+      if (nt < KT) load_tile(nt, nt % kNStages);
+      cp_commit();
+    }
+    const float* as = As + (kt % kNStages) * kNAStage;
+    const float* bs = Bs + (kt % kNStages) * kNBStage;
+    const int kvalid = min(kNBK, K - kt * kNBK);
+    if (kvalid == kNBK) {
+#pragma unroll
+      for (int kq = 0; kq < kNBK / 4; ++kq) {
+        float4 a[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          a[i] = *reinterpret_cast<const float4*>(as + (ty + 32 * i) * kNAStride + kq * 4);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          float av[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) av[i] = kk == 0 ? a[i].x : kk == 1 ? a[i].y : kk == 2 ? a[i].z : a[i].w;
+          step(av, bs + (kq * 4 + kk) * kNBStride);
+        }
+      }
+    } else {
+      // Ragged last k-tile: exactly kvalid steps, still in ascending k.
+      for (int kk = 0; kk < kvalid; ++kk) {
+        float av[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) av[i] = as[(ty + 32 * i) * kNAStride + kk];
+        step(av, bs + kk * kNBStride);
+      }
+    }
+  }
+  cp_wait<0>();
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty + 32 * i;
+    if (m >= M) continue;
+    float* crow = C + (long long)m * ldc + n0;
+    const int nl = N - n0;  // columns of this tile inside C
+#pragma unroll
+    for (int r = 0; r < 3; ++r) {
+      const int c = 32 * r + 4 * tx;
+      const f2 p0 = acc[i][2 * r], p1 = acc[i][2 * r + 1];
+      if (kVec && c + 3 < nl) {
+        *reinterpret_cast<float4*>(crow + c) = make_float4(f2_lo(p0), f2_hi(p0), f2_lo(p1), f2_hi(p1));
+      } else {
+        const float v[4] = {f2_lo(p0), f2_hi(p0), f2_lo(p1), f2_hi(p1)};
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (c + e < nl) crow[c + e] = v[e];
+      }
+    }
+    const int c = 96 + 2 * tx;
+    if (kVec && c + 1 < nl) {
+      *reinterpret_cast<float2*>(crow + c) = make_float2(f2_lo(acc[i][6]), f2_hi(acc[i][6]));
+    } else {
+      if (c < nl) crow[c] = f2_lo(acc[i][6]);
+      if (c + 1 < nl) crow[c + 1] = f2_hi(acc[i][6]);
+    }
+  }
+}
+
 // Launch `ntiles` parent tiles starting at tile_base, each as (128/BM)^2 CTAs.
 template <int BM, int BN, int BK, int STAGES, bool kVec>
 int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_t M, uint64_t N,
@@ -267,7 +444,8 @@ int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_
 
 template <bool kVec>
 int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M, uint64_t N,
-                    uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed, int acc_from_c) {
+                    uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed, int acc_from_c,
+                    int beside_collective) {
   const int tiles_n0 = (int)((N + 127) / 128);
   const int tiles = (int)((M + 127) / 128) * tiles_n0;
   // Whole waves of 128 x 128 CTAs (one per SM). The leftover tiles would run
@@ -280,10 +458,50 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
   // longer than the partial wave.
   const int waves = tiles / sms, rem = tiles - waves * sms;
   const bool split = rem > 0 && (4 * rem + sms - 1) / sms <= 2;
-  // (128 x 112 tiles, 37 per 4144 columns so that four row bands fill 148
-  // SMs, were measured too: with this kernel a wave of them takes as long as
-  // a wave of 128 x 128 tiles, so they never beat the plan above.)
   const int full = split ? waves * sms : tiles;
+  // The same site in 128 x 112 tiles costs ceil(tiles112 / sms) waves of
+  // kN112Wave each: a 128 x 112 CTA does 7/8 of a 128 x 128 CTA's work and
+  // was measured on B200 (N = K = 4096) at 0.905 of its time, 0.559 against
+  // 0.615 ms for a 512-row block (one wave each) and 4.35 against 4.21 ms
+  // for 4096 rows (8 waves against 7). It wins where the 128-wide plan ends
+  // in a part-filled wave that the narrower tiles fill: 512, 1024 and 1536 x
+  // 4096 blocks (0.91 / 1.82 / 2.73 against 1 / 2 / 3 waves; measured 9-10 %
+  // faster); 2048 x 4096 is a tie (3.64 against 3.65) and 4096 x 4096 stays
+  // on 128 x 128 tiles (7.28 against 7).
+  // Beside an SM-based collective (an NCCL kernel launched on another stream
+  // next to this multiply) the 128-wide plan stays when its part-filled wave
+  // leaves the collective at least kCollectiveSms SMs: the narrower tiles fill
+  // every SM in every wave, and the collective then waits for the multiply's
+  // end. Measured with the row-sharded 4096^2 site's B broadcast: at 4 GPUs
+  // (1024-row blocks, 40 SMs free in the second wave) keeping the 128-wide
+  // plan beside it took the step from 1.29 to 1.23 ms; at 8 GPUs (512-row
+  // blocks, 20 SMs free) the broadcast did not overlap either way and the
+  // narrower tiles' shorter multiply won (0.745 against 0.768 ms).
+  constexpr int kCollectiveSms = 32;
+  const int free_sms = rem > 0 && !split ? sms - rem : 0;
+  if (!(beside_collective && free_sms >= kCollectiveSms)) {
+    constexpr double kN112Wave = 0.91, kSplitWave = 0.65;
+    const int tiles_n112 = (int)((N + kNBN - 1) / kNBN);
+    const long long t112 = (long long)((M + 127) / 128) * tiles_n112;
+    const double cost128 = waves + (rem == 0 ? 0.0 : split ? kSplitWave : 1.0);
+    const double cost112 = (double)((t112 + sms - 1) / sms) * kN112Wave;
+    if (cost112 < cost128 - 0.01 && t112 <= 0x7fffffffll) {
+      auto kern = mm_strict_n112_kernel<kVec>;
+      static uint64_t attr_set = 0;
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (!(attr_set >> dev & 1)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNSmem);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(mm_strict_n112)");
+        attr_set |= 1ull << dev;
+      }
+      kern<<<(unsigned)t112, kNThreads, kNSmem, s>>>(A, B, C, (int)M, (int)N, (int)K, (long long)lda,
+                                                     (long long)ldb, (long long)ldc, seed, 0,
+                                                     (int)((M + 127) / 128), tiles_n112, acc_from_c, -0.0f);
+      count_launch();
+      return 0;
+    }
+  }
   MAPAL_TRY((launch_cfg<128, 128, 64, 2, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, full, tiles_n0,
                                                 acc_from_c)));
   return launch_cfg<64, 64, 16, 4, kVec>(s, A, B, C, M, N, K, lda, ldb, ldc, seed, full, tiles - full,
@@ -292,21 +510,21 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
 
 }  // namespace
 
-// The whole site as whole waves of 128 x 128 tiles plus a remainder in
-// 64 x 64 tiles. With acc_from_c, cells continue from the partial folds
-// stored in C (used to split K into ranges that overlap a B broadcast).
+// The whole site in the plan launch_balanced picks. With acc_from_c, cells
+// continue from the partial folds stored in C (used to split K into ranges
+// that overlap a B transfer).
 int launch_matmul_strict_ex(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
                             uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed,
-                            int acc_from_c) {
+                            int acc_from_c, int beside_collective) {
   if (M > 0x7fffffffull || N > 0x7fffffffull || K > 0x7fffffffull) return MAPAL_ERR_UNSUPPORTED;
   if ((M + 127) / 128 * ((N + 127) / 128) > 0x7fffffffull / 4) return MAPAL_ERR_UNSUPPORTED;
   const bool vec = aligned16(A) && aligned16(B) && aligned16(C) && lda % 4 == 0 && ldb % 4 == 0 &&
                    ldc % 4 == 0;
-  return vec ? launch_balanced<true>(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, acc_from_c)
-             : launch_balanced<false>(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, acc_from_c);
+  return vec ? launch_balanced<true>(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, acc_from_c, beside_collective)
+             : launch_balanced<false>(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, acc_from_c, beside_collective);
 }
 
 int launch_matmul_strict(cudaStream_t s, int sms, const float* A, const float* B, float* C, uint64_t M,
                          uint64_t N, uint64_t K, uint64_t lda, uint64_t ldb, uint64_t ldc, float seed) {
-  return launch_matmul_strict_ex(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, 0);
+  return launch_matmul_strict_ex(s, sms, A, B, C, M, N, K, lda, ldb, ldc, seed, 0, 0);
 }

@@ -100,7 +100,8 @@ int matmul_sharded_overlapped(MapalGpuCtx* ctx, const MapalTileSite* site, const
       if (m[i] == 0) continue;
       const uint64_t k0 = k_lo[c], kc = k_lo[c + 1] - k_lo[c];
       MAPAL_TRY(launch_matmul_strict_ex(d.stream, d.prof.sm_count, A[i] + k0, B[i] + site->b.base + k0 * ldb,
-                                        C[i], m[i], N, kc, lda, ldb, N, site->seed, c > 0 ? 1 : 0));
+                                        C[i], m[i], N, kc, lda, ldb, N, site->seed, c > 0 ? 1 : 0,
+                                        c + 1 < nchunks ? 1 : 0));
     }
   }
   return finish_all(ctx, false);

@@ -36,7 +36,9 @@ def _inputs(s, seed=11):
 @pytest.mark.parametrize("M,N,K", [(1, 1, 1), (77, 130, 33), (300, 257, 64), (1000, 260, 77),
                                    (1024, 1024, 256), (2049, 96, 40),
                                    # deep K: the strict path uploads and multiplies in k-range phases
-                                   (777, 300, 600), (1030, 513, 1000), (520, 64, 4096)])
+                                   (777, 300, 600), (1030, 513, 1000), (520, 64, 4096),
+                                   # 128 x 112 tiles, the later k-ranges continuing from C
+                                   (512, 2500, 700)])
 @pytest.mark.parametrize("pinned", [True, False])
 def test_strict_host_bit_exact(ctx, M, N, K, pinned):
     s = _site(M, N, K)

@@ -353,7 +353,10 @@ def test_matmul_known_answers(ctx, case):
 @pytest.mark.parametrize("M,N,K", [(5, 20, 7), (6, 32, 5), (33, 65, 70), (128, 128, 128), (1, 1, 1),
                                    (257, 129, 1000), (1024, 1024, 1024), (300, 4097, 19), (127, 128, 129),
                                    # row blocks of the sharded 4096^2 site (whole waves + 64x64 remainder)
-                                   (512, 4096, 64), (2048, 4096, 40), (1000, 4000, 33)])
+                                   (512, 4096, 64), (2048, 4096, 40), (1000, 4000, 33),
+                                   # 128 x 112 tiles (the plan for these row blocks), ragged rows,
+                                   # columns and k, a row stride that is not a multiple of 4
+                                   (500, 4000, 70), (1024, 4096, 130), (640, 3001, 70)])
 def test_matmul_random(ctx, M, N, K):
     A = o.gen(M * K, 0, 0)
     B = o.gen(K * N, 0, M * K)
@@ -386,6 +389,20 @@ def test_matmul_padded_rows_and_zero_signs(ctx):
     rc, want = o.tile_site(o.TileSite.from_buffer_copy(bytes(s)), A, B)
     assert rc == 0 and same_bits(host(C), want)
     assert np.all(host(C)[:N].view(np.uint32) == 0)
+
+
+def test_matmul_n112_padded_rows_and_zero_signs(ctx):
+    # 4 tile rows x 2500 columns: 92 tiles of 128 x 112 (one wave) against 80 of 128 x 128
+    M, N, K, lda, ldb = 512, 2500, 37, 41, 2503
+    A = o.gen(M * lda, 6, 0)
+    B = o.gen(K * ldb, 6, 99991)
+    A[:lda] = -0.0
+    s = fb.matmul_site(M, N, K, lda=lda, ldb=ldb)
+    s.seed = -0.0
+    C = empty_f32(M * N)
+    ctx.matmul(s, dev(A), dev(B), C)
+    rc, want = o.tile_site(o.TileSite.from_buffer_copy(bytes(s)), A, B)
+    assert rc == 0 and same_bits(host(C), want), first_diff(host(C), want)
 
 
 def test_matmul_k0_is_seed(ctx):

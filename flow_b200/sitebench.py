@@ -1,7 +1,7 @@
 """Micro-benchmark of one site class on one GPU (also the driver for ncu captures).
 
     python -m flow_b200.sitebench --site saxpy --n 1048576
-    python -m flow_b200.sitebench --site matmul --n 4096 [--mode tf32x3] --reps 3
+    python -m flow_b200.sitebench --site matmul --n 4096 [--rows 512] [--mode tf32x3] --reps 3
 
 Inputs are generated on the device from the seeded stream. Every launch
 reads data that is not in L2: the inputs are replicated into as many buffer
@@ -28,7 +28,8 @@ def _alloc(torch, n, dtype=None):
     return torch.empty(n, dtype=dtype or torch.float32, device="cuda")
 
 
-def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = fb.STRICT):
+def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = fb.STRICT,
+              rows: int | None = None):
     """Return (launch(set_index), bytes_per_launch, flops_per_launch, nsets_fn, extra)."""
     sets = []
     if name == "saxpy":
@@ -94,17 +95,20 @@ def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = f
         run = lambda s: ctx.conv2d_3x3(site, s[1], s[0], s[2])
         flops = 18 * (side - 2) ** 2
     elif name == "matmul":
+        # rows: an M x n block of the n x n site (one rank's row block of a
+        # row-sharded site); default the whole site
         kk = k or n
-        site = fb.matmul_site(n, n, kk)
+        m = rows or n
+        site = fb.matmul_site(m, n, kk)
 
         def mk(i):
-            A, B, C = _alloc(torch, n * kk), _alloc(torch, kk * n), _alloc(torch, n * n)
+            A, B, C = _alloc(torch, m * kk), _alloc(torch, kk * n), _alloc(torch, m * n)
             ctx.gen(A, 2, 0)
-            ctx.gen(B, 2, n * kk)
+            ctx.gen(B, 2, m * kk)
             return (A, B, C)
-        per = 4 * (2 * n * kk + n * n)
+        per = 4 * (m * kk + kk * n + m * n)
         run = lambda s: ctx.matmul(site, s[0], s[1], s[2], mode)
-        flops = 2 * n * n * kk
+        flops = 2 * m * n * kk
     elif name == "map_expr":
         # the benches' generator body as a general map program:
         # t -> (t * 7 + 13) % 101 - 50 -> widen_f32
@@ -186,8 +190,8 @@ def make_site(ctx, torch, name: str, n: int, k: int | None = None, mode: int = f
 
 def measure(ctx, torch, name: str, n: int, k: int | None = None, reps: int = 20, warmup: int = 3,
             mode: int = fb.STRICT, l2_bytes: int = 126 << 20, rotate: bool = True,
-            graph: bool = True) -> dict:
-    mk, run, per, flops = make_site(ctx, torch, name, n, k, mode)
+            graph: bool = True, rows: int | None = None) -> dict:
+    mk, run, per, flops = make_site(ctx, torch, name, n, k, mode, rows)
     nsets = max(1, math.ceil(2 * l2_bytes / per)) if rotate and per else 1
     sets = [mk(i) for i in range(nsets)]
     ctx.synchronize()
@@ -229,7 +233,7 @@ def measure(ctx, torch, name: str, n: int, k: int | None = None, reps: int = 20,
         torch.cuda.synchronize()
         ms = e0.elapsed_time(e1) / total
         del g
-    out = {"site": name, "n": n, "ms": ms, "bytes": per, "gbs": per / (ms * 1e-3) / 1e9 if per else None,
+    out = {"site": name, "n": n, **({"rows": rows} if rows else {}), "ms": ms, "bytes": per, "gbs": per / (ms * 1e-3) / 1e9 if per else None,
            "launches": total, "buffer_sets": nsets, "ms_host_issued": ms_host,
            "timing": "CUDA graph replay of the launches" if graph else "host-issued launches"}
     if flops:
@@ -242,6 +246,7 @@ def main() -> int:
     ap.add_argument("--site", choices=SITES + ("all",), default="all")
     ap.add_argument("--n", type=int, default=None, help="elements (side^2 for transpose/conv2d, side for matmul)")
     ap.add_argument("--k", type=int, default=None, help="taps (fir) or K (matmul)")
+    ap.add_argument("--rows", type=int, default=None, help="matmul: rows of the block (default n)")
     ap.add_argument("--reps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--mode", choices=["strict", "tf32x3"], default="strict")
@@ -260,7 +265,7 @@ def main() -> int:
         for s in sites:
             n = args.n or defaults[s]
             r = measure(ctx, torch, s, n, args.k, args.reps, args.warmup, mode, l2, not args.no_rotate,
-                        not args.no_graph)
+                        not args.no_graph, args.rows if s == "matmul" else None)
             print(json.dumps(r), flush=True)
     return 0
 

@@ -33,8 +33,18 @@ struct NcclApi {
   int (*GroupEnd)() = nullptr;
   const char* (*GetErrorString)(int) = nullptr;
   int (*AllGather)(const void*, void*, size_t, int, ncclComm_t, cudaStream_t) = nullptr;
+  // optional (NCCL >= 2.14): rank init with a config, used to cap the CTAs
+  int (*CommInitRankConfig)(ncclComm_t*, int, NcclId, int, void*) = nullptr;
 };
 NcclApi* nccl_api();  // loads on first use; check ->loaded
+
+// The most CTAs a rank communicator's collectives use (NCCL's maxCTAs). A
+// collective launched beside a multiply runs in the SMs the multiply's
+// part-filled wave leaves free, and completes only when all its CTAs have
+// run, so it must fit there: the strict matmul's plan keeps at least this
+// many SMs free beside a collective (20 at the row-sharded 4096^2 site's
+// 8-GPU block, 40 at its 4-GPU block).
+constexpr int kCollectiveCtas = 16;
 
 // ---- peer exchange --------------------------------------------------------------
 // The sharded sum combines its per-rank partials over peer memory inside the

@@ -13,6 +13,8 @@
 #include <atomic>
 #include <mutex>
 
+#include <climits>
+
 #include "common.cuh"
 
 // ---- errors -------------------------------------------------------------------
@@ -75,6 +77,7 @@ NcclApi* nccl_api() {
       g_nccl.error = "libnccl.so.2 lacks a required symbol";
       return;
     }
+    g_nccl.CommInitRankConfig = (int (*)(ncclComm_t*, int, NcclId, int, void*))dlsym(h, "ncclCommInitRankConfig");
     g_nccl.loaded = true;
   });
   return &g_nccl;
@@ -273,7 +276,23 @@ extern "C" int mapal_gpu_ctx_create_rank(int device, int nranks, int rank, const
     }
     NcclId u;
     memcpy(u.internal, id, 128);
-    rc = n->CommInitRank(&ctx->dev[0].comm, nranks, u, rank);
+    if (n->CommInitRankConfig) {
+      // The config as NCCL 2.14 laid it out (NCCL reads a config by its size
+      // and version fields, so later libraries take it and keep their
+      // defaults for the fields it lacks); only maxCTAs is set.
+      struct {
+        size_t size;
+        unsigned int magic, version;
+        int blocking, cgaClusterSize, minCTAs, maxCTAs;
+        const char* netName;
+      } cfg = {sizeof(cfg), 0xcafebeefu, 2 * 10000 + 14 * 100, INT_MIN, INT_MIN, INT_MIN, kCollectiveCtas, nullptr};
+      rc = n->CommInitRankConfig(&ctx->dev[0].comm, nranks, u, rank, &cfg);
+      // a library that rejects the config (ncclInvalidArgument, raised while
+      // the config is read, before any rank connects) gets a plain init
+      if (rc == 4) rc = n->CommInitRank(&ctx->dev[0].comm, nranks, u, rank);
+    } else {
+      rc = n->CommInitRank(&ctx->dev[0].comm, nranks, u, rank);
+    }
     if (rc) {
       mapal_gpu_ctx_destroy(ctx);
       return nccl_fail(rc, "ncclCommInitRank");

@@ -470,16 +470,13 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
   // on 128 x 128 tiles (7.28 against 7).
   // Beside an SM-based collective (an NCCL kernel launched on another stream
   // next to this multiply) the 128-wide plan stays when its part-filled wave
-  // leaves the collective at least kCollectiveSms SMs: the narrower tiles fill
-  // every SM in every wave, and the collective then waits for the multiply's
-  // end. Measured with the row-sharded 4096^2 site's B broadcast: at 4 GPUs
-  // (1024-row blocks, 40 SMs free in the second wave) keeping the 128-wide
-  // plan beside it took the step from 1.29 to 1.23 ms; at 8 GPUs (512-row
-  // blocks, 20 SMs free) the broadcast did not overlap either way and the
-  // narrower tiles' shorter multiply won (0.745 against 0.768 ms).
-  constexpr int kCollectiveSms = 32;
+  // leaves the collective kCollectiveCtas SMs, its CTA cap: the narrower tiles
+  // fill every SM in every wave, and the collective then waits for the
+  // multiply's end. Measured with the row-sharded 4096^2 site's B broadcast
+  // at 4 GPUs (1024-row blocks, 40 SMs free in the second wave): keeping the
+  // 128-wide plan beside it took the step from 1.29 to 1.23 ms.
   const int free_sms = rem > 0 && !split ? sms - rem : 0;
-  if (!(beside_collective && free_sms >= kCollectiveSms)) {
+  if (!(beside_collective && free_sms >= kCollectiveCtas)) {
     constexpr double kN112Wave = 0.91, kSplitWave = 0.65;
     const int tiles_n112 = (int)((N + kNBN - 1) / kNBN);
     const long long t112 = (long long)((M + 127) / 128) * tiles_n112;

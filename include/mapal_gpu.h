@@ -186,7 +186,10 @@ int mapal_gpu_ctx_create(uint32_t device_mask, MapalGpuCtx** out);
 
 /* Create a context for one rank of a multi-process job (one process per GPU).
  * All ranks pass the same 128-byte id, made once by
- * mapal_gpu_nccl_unique_id() on one rank and shared by the caller. */
+ * mapal_gpu_nccl_unique_id() on one rank and shared by the caller. The
+ * rank's communicator caps its collectives at 16 CTAs (NCCL maxCTAs, where
+ * the loaded NCCL has ncclCommInitRankConfig), so a collective overlapped
+ * with a multiply fits in the SMs the multiply leaves free. */
 int mapal_gpu_nccl_unique_id(uint8_t id[128]);
 int mapal_gpu_ctx_create_rank(int device, int nranks, int rank, const uint8_t id[128],
                               MapalGpuCtx** out);

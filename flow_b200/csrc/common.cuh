@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 #include <vector>
 
@@ -137,6 +138,21 @@ int cuda_fail(cudaError_t e, const char* what);
     int _rc = (expr);            \
     if (_rc != 0) return _rc;    \
   } while (0)
+
+// Raise a kernel's dynamic shared-memory limit on the current device (device
+// number `device`) the first time it is launched there. `done` keeps one bit
+// per device; two host threads launching first at once may both set the
+// attribute, which is harmless (the value is the same). Devices beyond 63 set
+// it on every launch.
+inline int ensure_smem_attr(std::atomic<uint64_t>& done, const void* kernel, int device, size_t bytes,
+                            const char* what) {
+  const uint64_t bit = device >= 0 && device < 64 ? 1ull << device : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return 0;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  done.fetch_or(bit, std::memory_order_release);
+  return 0;
+}
 
 // One kernel launch issued by this library (process-wide count, read by
 // mapal_gpu_launch_count).

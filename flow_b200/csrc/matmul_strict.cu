@@ -424,14 +424,10 @@ int launch_cfg(cudaStream_t s, const float* A, const float* B, float* C, uint64_
                int tiles_n0, int acc_from_c) {
   using G = Cfg<BM, BN, BK, 8, 8, STAGES>;
   auto kern = mm_strict_kernel<BM, BN, BK, 8, 8, STAGES, kVec>;
-  static uint64_t attr_set = 0;  // per template instance, one bit per device
+  static std::atomic<uint64_t> attr_set{0};  // per template instance, one bit per device
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (!(attr_set >> dev & 1)) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)G::kSmem);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(mm_strict)");
-    attr_set |= 1ull << dev;
-  }
+  MAPAL_CUDA(cudaGetDevice(&dev));
+  MAPAL_TRY(ensure_smem_attr(attr_set, (const void*)kern, dev, G::kSmem, "cudaFuncSetAttribute(mm_strict)"));
   constexpr int kSplit = 128 / BM;
   const unsigned grid = (unsigned)ntiles * kSplit * kSplit;
   if (grid == 0) return 0;
@@ -484,14 +480,10 @@ int launch_balanced(cudaStream_t s, int sms, const float* A, const float* B, flo
     const double cost112 = (double)((t112 + sms - 1) / sms) * kN112Wave;
     if (cost112 < cost128 - 0.01 && t112 <= 0x7fffffffll) {
       auto kern = mm_strict_n112_kernel<kVec>;
-      static uint64_t attr_set = 0;
+      static std::atomic<uint64_t> attr_set{0};
       int dev = 0;
-      cudaGetDevice(&dev);
-      if (!(attr_set >> dev & 1)) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kNSmem);
-        if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(mm_strict_n112)");
-        attr_set |= 1ull << dev;
-      }
+      MAPAL_CUDA(cudaGetDevice(&dev));
+      MAPAL_TRY(ensure_smem_attr(attr_set, (const void*)kern, dev, kNSmem, "cudaFuncSetAttribute(mm_strict_n112)"));
       kern<<<(unsigned)t112, kNThreads, kNSmem, s>>>(A, B, C, (int)M, (int)N, (int)K, (long long)lda,
                                                      (long long)ldb, (long long)ldc, seed, 0,
                                                      (int)((M + 127) / 128), tiles_n112, acc_from_c, -0.0f);

@@ -759,15 +759,17 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
+// The driver's cuTensorMapEncodeTiled, looked up once (a function-local
+// static is initialised exactly once, also when threads race to it).
 EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
+  static const EncodeTiledFn fn = [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
     if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
-      fn = (EncodeTiledFn)p;
-  }
+      return (EncodeTiledFn)p;
+    return (EncodeTiledFn) nullptr;
+  }();
   return fn;
 }
 
@@ -840,11 +842,9 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
     MAPAL_TRY(make_map(&m_bhi, bhi, N, K, kp, BN));
     MAPAL_TRY(make_map(&m_blo, blo, N, K, kp, BN));
     const size_t smem = sizeof(SmemF) + 1024;
-    static uint64_t attr_fused = 0;
-    if (!(attr_fused >> d.device & 1)) {
-      MAPAL_CUDA(cudaFuncSetAttribute(mm_tf32x3_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      attr_fused |= 1ull << d.device;
-    }
+    static std::atomic<uint64_t> attr_fused{0};
+    MAPAL_TRY(ensure_smem_attr(attr_fused, (const void*)mm_tf32x3_fused_kernel, d.device, smem,
+                               "cudaFuncSetAttribute(mm_tf32x3_fused_kernel)"));
     if (whole > 0) {
       mm_tf32x3_fused_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(
           m_a, m_bhi, m_blo, C, (int)M, (int)N, (int)K, (long long)ldc, seed, d.trap, tiles_m, tiles_n, 0, 1, nullptr);
@@ -875,11 +875,9 @@ int launch_matmul_tf32x3(DeviceSlot& d, const float* A, const float* B, float* C
   MAPAL_TRY(make_map(&m_blo, blo, N, K, kp, BN));
 
   const size_t smem = sizeof(Smem) + 1024;
-  static uint64_t attr_set = 0;
-  if (!(attr_set >> d.device & 1)) {
-    MAPAL_CUDA(cudaFuncSetAttribute(mm_tf32x3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_set |= 1ull << d.device;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  MAPAL_TRY(ensure_smem_attr(attr_set, (const void*)mm_tf32x3_kernel, d.device, smem,
+                             "cudaFuncSetAttribute(mm_tf32x3_kernel)"));
   if (whole > 0) {
     mm_tf32x3_kernel<<<(unsigned)whole, kThreads, smem, d.stream>>>(m_ahi, m_alo, m_bhi, m_blo, C, (int)M, (int)N,
                                                                     (int)K, (long long)ldc, seed, d.trap, tiles_m,
@@ -910,11 +908,9 @@ extern "C" int mapal_gpu_probe_mma_peak(MapalGpuCtx* ctx, int kind, uint32_t ite
   DeviceSlot& d = ctx->dev[0];
   // 120 KiB of dynamic shared memory: only one probe CTA fits on an SM
   const size_t smem = 120 * 1024;
-  static uint64_t attr_set = 0;
-  if (!(attr_set >> d.device & 1)) {
-    MAPAL_CUDA(cudaFuncSetAttribute(probe_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_set |= 1ull << d.device;
-  }
+  static std::atomic<uint64_t> attr_set{0};
+  MAPAL_TRY(ensure_smem_attr(attr_set, (const void*)probe_mma_kernel, d.device, smem,
+                             "cudaFuncSetAttribute(probe_mma_kernel)"));
   MAPAL_TRY(arena_reserve(d, (size_t)d.prof.sm_count * sizeof(float)));
   float* sink = static_cast<float*>(d.arena);
   cudaEvent_t e0, e1;
